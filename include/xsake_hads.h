@@ -1,0 +1,149 @@
+/*
+ * xsake_hads.h -- C ABI of libxsake_hads.so, the sm_100a (B200) implementation of the
+ * HADS block-sparse attention path of Hridambiswas/XSAKE.
+ *
+ * The reference exposes this path as Python/JAX functions; each entry point below names
+ * the reference function it replaces (path:line inside the reference project).  A JAX
+ * FFI handler, a ctypes stub or a C++ caller binds these symbols directly.
+ *
+ * Conventions
+ *   - Every pointer argument named *_dev is DEVICE memory owned by the caller.
+ *   - Calls are stream-ordered on `stream` (a cudaStream_t passed as void*; NULL = the
+ *     legacy default stream), never synchronise the host, and never allocate: scratch
+ *     comes from a caller-provided workspace whose size the *_workspace_size query gives.
+ *   - Return value: XSAKE_OK (0) or an XSAKE_E* code; xsake_last_error() then returns a
+ *     message for the calling thread.  Argument errors are detected before any launch.
+ *   - Tensors of the attention path use the layout [B, H, S, D] addressed through
+ *     element strides (stride of D must be 1), so both [B,H,S,D] and [B,S,H,D] work.
+ *   - dtype codes: XSAKE_F32 (float32), XSAKE_BF16 (bfloat16).
+ */
+#ifndef XSAKE_HADS_H
+#define XSAKE_HADS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define XSAKE_API __attribute__((visibility("default")))
+#else
+#define XSAKE_API
+#endif
+
+#define XSAKE_ABI_VERSION 1
+
+enum {
+  XSAKE_OK = 0,
+  XSAKE_EINVAL = 1,        /* bad shape, dtype, pointer, alignment or workspace size    */
+  XSAKE_EUNSUPPORTED = 2,  /* valid request outside what the kernels implement           */
+  XSAKE_ECUDA = 3,         /* a CUDA runtime/driver call failed                          */
+  XSAKE_ETIMEOUT = 4,      /* a bounded device-side wait gave up (see xsake_device_error) */
+  XSAKE_EDEVICE = 5        /* a kernel recorded an error flag (see xsake_device_error)   */
+};
+
+enum { XSAKE_F32 = 0, XSAKE_BF16 = 1 };
+
+/* ------------------------------------------------------------------ library status  */
+XSAKE_API int xsake_abi_version(void);
+XSAKE_API const char* xsake_last_error(void);
+/* Reads and clears the device-side error word of the current device after
+ * synchronising `stream`.  *code = 0 when no kernel recorded an error; otherwise a
+ * packed (kind << 24 | detail) value.  Returns XSAKE_OK or XSAKE_ECUDA. */
+XSAKE_API int xsake_device_error(void* stream, int32_t* code);
+
+/* ------------------------------------------------------------------ block-mask plans
+ * Replaces the per-call mask handling of the reference:
+ *   _broadcast_mask                 kernels/pallas/sparse_attention.py:286-298
+ *   token-mask expansion + causal   kernels/pallas/sparse_attention.py:76-81
+ * A plan is compiled once per (mask, B, H, S, block_size, causal) and reused by every
+ * attention call with that mask.  mask_dev is uint8 0/1 [mask_batch, mask_heads, nq, nk]
+ * with mask_batch in {1, B}, mask_heads in {1, H}, nq = nk = S / block_size. */
+typedef struct {
+  int32_t batch, heads, seq;
+  int32_t mask_batch, mask_heads;
+  int32_t block_size;
+  int32_t causal;
+} XsakeMaskDims;
+
+XSAKE_API int xsake_mask_plan_bytes(const XsakeMaskDims* dims, size_t* bytes);
+XSAKE_API int xsake_mask_compile(const XsakeMaskDims* dims, const uint8_t* mask_dev, void* plan_dev,
+                       size_t plan_bytes, void* stream);
+/* Copies the plan's summary to host (synchronises `stream`): out[0] = active (q-block,
+ * kv-block) pairs after the causal cut over B*H, out[1] = 64x64 tiles the forward
+ * computes, out[2] = fully masked q-blocks, out[3] = forward work items. */
+XSAKE_API int xsake_mask_plan_stats(const void* plan_dev, void* stream, int64_t out[4]);
+
+/* ------------------------------------------------------------------ attention
+ * Replaces sparse_attention / sparse_attention_pallas / _sparse_attn_fwd_kernel
+ * (kernels/pallas/sparse_attention.py:96-156, :161-252, :257-281) with the output
+ * semantics of sparse_attention_reference (:45-91): token-level causal mask, and a fully
+ * masked query row attends uniformly to all S keys (finfo.min fill).  lse[b,h,s] is the
+ * natural-log row normaliser (finfo(float32).min for fully masked rows). */
+typedef struct {
+  int32_t dtype;            /* XSAKE_F32 or XSAKE_BF16 (q, k, v, o, do, dq, dk, dv)   */
+  int32_t batch, heads, seq, head_dim;
+  int32_t block_size;
+  int32_t causal;
+  int32_t mask_batch;       /* leading dims of the mask the plan was compiled from     */
+  int32_t mask_heads;
+  float scale;              /* softmax scale; <= 0 selects 1/sqrt(head_dim)           */
+  int64_t q_stride[3];      /* element strides of (b, h, s); d stride is 1            */
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];      /* also used for do, dq, dk, dv                           */
+} XsakeAttnDesc;
+
+XSAKE_API int xsake_attn_fwd_workspace_size(const XsakeAttnDesc* desc, size_t* bytes);
+XSAKE_API int xsake_attn_fwd(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
+                   const void* k_dev, const void* v_dev, void* o_dev, float* lse_dev,
+                   void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/* Backward of the above (the reference has no VJP; this is autodiff of
+ * sparse_attention_reference, :45-91).  lse_dev is the forward's output. */
+XSAKE_API int xsake_attn_bwd_workspace_size(const XsakeAttnDesc* desc, size_t* bytes);
+XSAKE_API int xsake_attn_bwd(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
+                   const void* k_dev, const void* v_dev, const void* o_dev,
+                   const float* lse_dev, const void* do_dev, void* dq_dev, void* dk_dev,
+                   void* dv_dev, void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ row kernels
+ * fused_softmax / fused_softmax_pallas / _softmax_kernel
+ * (kernels/pallas/fused_softmax.py:26-87): softmax over the last axis of a contiguous
+ * [rows, cols] array, fp32 statistics, output in the input dtype. */
+XSAKE_API int xsake_softmax_fwd(int32_t dtype, int64_t rows, int64_t cols, const void* x_dev,
+                      void* y_dev, void* stream);
+/* dx = y * (dy - sum(dy * y)) -- autodiff of the above. */
+XSAKE_API int xsake_softmax_bwd(int32_t dtype, int64_t rows, int64_t cols, const void* y_dev,
+                      const void* dy_dev, void* dx_dev, void* stream);
+
+/* fused_layernorm / fused_layernorm_pallas / _layernorm_kernel
+ * (kernels/pallas/fused_layernorm.py:26-119): x [rows, d] in x_dtype, gamma/beta fp32
+ * [d], fp32 two-pass statistics, y in x_dtype.  mean_dev / rstd_dev may be NULL. */
+XSAKE_API int xsake_layernorm_fwd(int32_t x_dtype, int64_t rows, int64_t d, const void* x_dev,
+                        const float* gamma_dev, const float* beta_dev, float eps,
+                        void* y_dev, float* mean_dev, float* rstd_dev, void* stream);
+XSAKE_API int xsake_layernorm_bwd_workspace_size(int64_t rows, int64_t d, size_t* bytes);
+/* dgamma / dbeta are fp32 [d] and are overwritten (deterministic column reduction). */
+XSAKE_API int xsake_layernorm_bwd(int32_t x_dtype, int64_t rows, int64_t d, const void* x_dev,
+                        const float* gamma_dev, const float* mean_dev, const float* rstd_dev,
+                        const void* dy_dev, void* dx_dev, float* dgamma_dev, float* dbeta_dev,
+                        void* workspace_dev, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ HADS calibration
+ * compute_attention_entropy (kernels/hads/hads_pattern.py:36-50): p fp32
+ * [B, H, Sq, Sk] contiguous; head_sums_dev[h] (fp64) receives sum over (b, q) of
+ * -sum_k clip(p,1e-9,1) * log(clip(p,1e-9,1)).  The caller divides by B*Sq for the mean,
+ * or all-reduces the sums across ranks first.  Deterministic (fixed reduction order). */
+XSAKE_API int xsake_entropy_workspace_size(int64_t batch, int64_t heads, int64_t sq, size_t* bytes);
+XSAKE_API int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t heads, int64_t sq,
+                       int64_t sk, double* head_sums_dev, void* workspace_dev,
+                       size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XSAKE_HADS_H */

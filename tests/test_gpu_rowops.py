@@ -1,0 +1,148 @@
+"""GPU parity of the row kernels and the calibration entropy against the oracle.
+
+Tolerances: softmax fp32 rtol 1e-5 / atol 1e-6 (tests/test_kernel_correctness.py:101-117 in the
+reference); LayerNorm fp32 rtol 1e-4 / atol 1e-5 (:122-148); bf16 outputs 2e-2 relative to the
+largest reference magnitude; entropies 1e-5 relative.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from oracle import hads as oh  # noqa: E402
+from oracle import inputs as oi  # noqa: E402
+from oracle import rowops as orow  # noqa: E402
+
+G = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_softmax_golden_and_masked_rows():
+    from xsake_b200.fused_softmax import fused_softmax
+    z = np.load(os.path.join(G, "rowops.npz"))
+    np.testing.assert_allclose(fused_softmax(z["sm_x"]), z["sm_out"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(fused_softmax(z["sm_xm"]), z["sm_outm"], rtol=1e-5, atol=1e-6)
+    s = fused_softmax(np.random.default_rng(0).standard_normal((4, 128)).astype(np.float32))
+    np.testing.assert_allclose(s.sum(-1), np.ones(4), atol=1e-5)
+
+
+@pytest.mark.parametrize("cols", [1, 7, 33, 100, 1024, 1536, 4096, 5000])
+def test_softmax_shapes_fp32(cols):
+    from xsake_b200.fused_softmax import fused_softmax
+    x = np.random.default_rng(cols).standard_normal((37, cols)).astype(np.float32) * 3
+    np.testing.assert_allclose(fused_softmax(x), orow.softmax(x), rtol=1e-5, atol=1e-6)
+
+
+def test_softmax_all_masked_row_is_nan_like_reference():
+    from xsake_b200.fused_softmax import fused_softmax
+    x = np.zeros((3, 64), np.float32)
+    x[1] = -np.inf
+    y = fused_softmax(x)
+    assert np.isnan(y[1]).all() and np.isfinite(y[[0, 2]]).all()
+
+
+def test_softmax_config1_full_size():
+    """Config 1a: fp32 [98304, 1024] ~ N(0, 2^2) with causal -inf masking."""
+    from xsake_b200.fused_softmax import softmax_forward
+    x = oi.softmax_logits()
+    y = softmax_forward(torch.from_numpy(x).cuda()).cpu().numpy()
+    ref = orow.softmax(x)
+    np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-6)
+
+
+def test_softmax_bf16_and_backward():
+    from xsake_b200.fused_softmax import softmax_backward, softmax_forward
+    x = np.random.default_rng(1).standard_normal((64, 1000)).astype(np.float32)
+    xb = oi.to_bf16(x).astype(np.float32)
+    y = softmax_forward(torch.from_numpy(xb).to(torch.bfloat16).cuda()).float().cpu().numpy()
+    ref = orow.softmax(xb)
+    assert np.abs(y - ref).max() <= 2e-2 * np.abs(ref).max()
+    dy = np.random.default_rng(2).standard_normal((64, 1000)).astype(np.float32)
+    yt = torch.from_numpy(orow.softmax(x).astype(np.float32)).cuda()
+    dx = softmax_backward(yt, torch.from_numpy(dy).cuda()).cpu().numpy()
+    np.testing.assert_allclose(dx, orow.softmax_backward(yt.cpu().numpy(), dy), rtol=1e-5, atol=1e-6)
+
+
+def test_layernorm_golden():
+    from xsake_b200.fused_layernorm import fused_layernorm
+    z = np.load(os.path.join(G, "rowops.npz"))
+    np.testing.assert_allclose(fused_layernorm(z["ln_x"], z["ln_g"], z["ln_b"]), z["ln_out"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(fused_layernorm(z["ln_x"], z["ln_g"], z["ln_b"], eps=1e-2), z["ln_out_eps"],
+                               rtol=1e-4, atol=1e-5)
+    m = fused_layernorm(z["ln_x"], np.ones(128, np.float32), np.zeros(128, np.float32)).mean(-1)
+    np.testing.assert_allclose(m, np.zeros_like(m), atol=1e-4)
+
+
+@pytest.mark.parametrize("d", [64, 100, 768, 1024, 3000])
+def test_layernorm_shapes(d):
+    from xsake_b200.fused_layernorm import fused_layernorm
+    rng = np.random.default_rng(d)
+    x = rng.standard_normal((19, d)).astype(np.float32) * 2 + 1
+    g, b = rng.standard_normal(d).astype(np.float32), rng.standard_normal(d).astype(np.float32)
+    np.testing.assert_allclose(fused_layernorm(x, g, b), orow.layernorm(x, g, b), rtol=1e-4, atol=1e-5)
+
+
+def test_layernorm_config1_bf16():
+    """Config 1b: bf16 [8192, 768], fp32 gamma/beta/statistics, eps 1e-5, bf16 output."""
+    from xsake_b200.fused_layernorm import layernorm_forward
+    x, g, b = oi.layernorm_inputs()
+    xt = torch.from_numpy(np.asarray(x).view(np.int16)).view(torch.bfloat16).cuda()
+    y, mean, rstd = layernorm_forward(xt, torch.from_numpy(g), torch.from_numpy(b), 1e-5, return_stats=True)
+    assert y.dtype == torch.bfloat16
+    ref, rm, rr = orow.layernorm(np.asarray(x, np.float32), g, b, return_stats=True)
+    assert np.abs(y.float().cpu().numpy() - ref).max() <= 2e-2 * np.abs(ref).max()
+    np.testing.assert_allclose(mean.cpu().numpy(), rm, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(rstd.cpu().numpy(), rr, rtol=1e-4)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_layernorm_backward(dtype):
+    from xsake_b200.fused_layernorm import layernorm_backward, layernorm_forward
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((300, 768)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(768)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(768)).astype(np.float32)
+    dy = rng.standard_normal((300, 768)).astype(np.float32)
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    if dtype == "bf16":
+        x, dy = oi.to_bf16(x).astype(np.float32), oi.to_bf16(dy).astype(np.float32)
+    xt, dyt = torch.from_numpy(x).to(tdt).cuda(), torch.from_numpy(dy).to(tdt).cuda()
+    _, mean, rstd = layernorm_forward(xt, torch.from_numpy(g), torch.from_numpy(b), return_stats=True)
+    dx, dg, db = layernorm_backward(xt, torch.from_numpy(g).cuda(), mean, rstd, dyt)
+    rdx, rdg, rdb = orow.layernorm_backward(x, g, dy)
+    if dtype == "f32":
+        np.testing.assert_allclose(dx.cpu().numpy(), rdx, rtol=1e-4, atol=1e-4)
+    else:
+        assert np.abs(dx.float().cpu().numpy() - rdx).max() <= 2e-2 * np.abs(rdx).max()
+    np.testing.assert_allclose(dg.cpu().numpy(), rdg, rtol=1e-4, atol=1e-3)
+    np.testing.assert_allclose(db.cpu().numpy(), rdb, rtol=1e-4, atol=1e-3)
+
+
+def test_entropy_golden_and_profile():
+    from xsake_b200 import hads_pattern as hp
+    z = np.load(os.path.join(G, "calibration.npz"))
+    for a in ("attn", "attn2"):
+        got = hp.compute_attention_entropy(z[a]).astype(np.float64)
+        want = z["entropy_" + a].astype(np.float64)
+        assert np.max(np.abs(got - want) / np.abs(want)) <= 1e-5
+    prof = hp.build_hads_profile([z["attn"], z["attn2"]], seq_len=128, block_size=16, causal=True)
+    np.testing.assert_allclose(prof.head_entropies, z["profile_ent"], rtol=1e-5)
+    np.testing.assert_array_equal(prof.block_masks, z["profile_mask"])
+
+
+def test_entropy_calibration_batch():
+    """One config-2 style batch (B=2 here to bound host memory) of non-causal softmax P."""
+    from xsake_b200 import hads_pattern as hp
+    q, k = oi.calibration_batch(0, batch=2)
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) / np.float32(8.0)
+    p = orow.softmax(s).astype(np.float32)
+    got = hp.compute_attention_entropy(torch.from_numpy(p).cuda()).cpu().numpy().astype(np.float64)
+    want = oh.compute_attention_entropy(p)
+    assert np.max(np.abs(got - want) / np.abs(want)) <= 1e-5
+    sums = hp.entropy_head_sums(torch.from_numpy(p).cuda())
+    s2 = hp.entropy_head_sums(torch.from_numpy(p).cuda())
+    assert torch.equal(sums, s2)                      # deterministic reduction order

@@ -1,0 +1,123 @@
+// HADS calibration: per-head Shannon entropy of materialised attention probabilities.
+// Replaces compute_attention_entropy (kernels/hads/hads_pattern.py:36-50):
+//   H[b,h,q] = -sum_k clip(p,1e-9,1) * log(clip(p,1e-9,1)),  reduced over (b, q) per head.
+// HBM-bound: every probability is read once with 16-byte loads; each warp owns one row and
+// reduces it with shuffles; rows are summed in fp64 in a fixed order (per-CTA partials in the
+// workspace, then one pass per head), so the result is bitwise reproducible.
+#include "common.cuh"
+
+#include <algorithm>
+
+XSAKE_DEFINE_DEVICE_ERROR(entropy)
+
+namespace xsake {
+namespace {
+
+constexpr int kEntWarps = 8;
+constexpr float kClipLo = 1e-9f;
+
+__device__ __forceinline__ float plogp(float p) {
+  p = fminf(fmaxf(p, kClipLo), 1.0f);
+  return p * __log2f(p);
+}
+
+struct EntropyGeom {
+  int64_t B, H, Sq, Sk;
+  int64_t rows_per_cta;   // divides Sq so a CTA never straddles two (b, h) slices
+  int64_t ctas_per_bh;
+};
+
+// Rows of one CTA: [cta * rows_per_cta, +rows_per_cta) of the flattened [B*H*Sq] rows.
+__global__ void __launch_bounds__(256) entropy_rows_kernel(const float* __restrict__ p, EntropyGeom g,
+                                                           double* __restrict__ partial) {
+  __shared__ double swarp[kEntWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row0 = (int64_t)blockIdx.x * g.rows_per_cta;
+  double acc = 0.0;
+  const bool vec = (g.Sk % 4) == 0;
+  for (int64_t r = warp; r < g.rows_per_cta; r += kEntWarps) {
+    const float* pr = p + (row0 + r) * g.Sk;
+    float s = 0.f;
+    if (vec) {
+      const float4* p4 = reinterpret_cast<const float4*>(pr);
+      const int64_t nv = g.Sk / 4;
+      int64_t v = lane;
+      for (; v + 96 < nv; v += 128) {
+        const float4 a = p4[v], b = p4[v + 32], c = p4[v + 64], d = p4[v + 96];
+        s += plogp(a.x) + plogp(a.y) + plogp(a.z) + plogp(a.w);
+        s += plogp(b.x) + plogp(b.y) + plogp(b.z) + plogp(b.w);
+        s += plogp(c.x) + plogp(c.y) + plogp(c.z) + plogp(c.w);
+        s += plogp(d.x) + plogp(d.y) + plogp(d.z) + plogp(d.w);
+      }
+      for (; v < nv; v += 32) {
+        const float4 a = p4[v];
+        s += plogp(a.x) + plogp(a.y) + plogp(a.z) + plogp(a.w);
+      }
+    } else {
+      for (int64_t c = lane; c < g.Sk; c += 32) s += plogp(pr[c]);
+    }
+    s = warp_sum(s);
+    acc += -(double)s * (double)kLn2;
+  }
+  if (lane == 0) swarp[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < kEntWarps; ++w) t += swarp[w];
+    partial[blockIdx.x] = t;
+  }
+}
+
+__global__ void entropy_heads_kernel(const double* __restrict__ partial, EntropyGeom g, double* __restrict__ head_sums) {
+  const int h = blockIdx.x * blockDim.x + threadIdx.x;
+  if (h >= g.H) return;
+  double t = 0.0;
+  for (int64_t b = 0; b < g.B; ++b)
+    for (int64_t c = 0; c < g.ctas_per_bh; ++c) t += partial[(b * g.H + h) * g.ctas_per_bh + c];
+  head_sums[h] = t;
+}
+
+EntropyGeom geom(int64_t B, int64_t H, int64_t Sq, int64_t Sk) {
+  EntropyGeom g{B, H, Sq, Sk, 1, 1};
+  // Aim for ~64 rows per CTA, keeping rows_per_cta a divisor of Sq.
+  int64_t rpc = 1;
+  for (int64_t c = std::min<int64_t>(64, Sq); c >= 1; --c)
+    if (Sq % c == 0) { rpc = c; break; }
+  g.rows_per_cta = rpc;
+  g.ctas_per_bh = Sq / rpc;
+  return g;
+}
+
+}  // namespace
+}  // namespace xsake
+
+using namespace xsake;
+
+extern "C" int xsake_entropy_workspace_size(int64_t batch, int64_t heads, int64_t sq, size_t* bytes) {
+  clear_error();
+  XSAKE_REQUIRE(bytes && batch > 0 && heads > 0 && sq > 0, XSAKE_EINVAL, "bad arguments");
+  const EntropyGeom g = geom(batch, heads, sq, 1);
+  *bytes = (size_t)(batch * heads * g.ctas_per_bh) * sizeof(double);
+  return XSAKE_OK;
+}
+
+extern "C" int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t heads, int64_t sq, int64_t sk,
+                                  double* head_sums_dev, void* workspace_dev, size_t workspace_bytes,
+                                  void* stream) {
+  clear_error();
+  XSAKE_REQUIRE(batch > 0 && heads > 0 && sq > 0 && sk > 0, XSAKE_EINVAL, "dims must be positive");
+  XSAKE_REQUIRE(p_dev && head_sums_dev, XSAKE_EINVAL, "NULL pointer");
+  XSAKE_REQUIRE(((uintptr_t)p_dev & 15) == 0, XSAKE_EINVAL, "p must be 16-byte aligned");
+  const EntropyGeom g = geom(batch, heads, sq, sk);
+  const int64_t nctas = batch * heads * g.ctas_per_bh;
+  XSAKE_REQUIRE(nctas < (1ll << 31), XSAKE_EUNSUPPORTED, "too many rows");
+  XSAKE_REQUIRE(workspace_dev && workspace_bytes >= (size_t)nctas * sizeof(double), XSAKE_EINVAL,
+                "workspace too small: %zu < %zu bytes", workspace_bytes, (size_t)nctas * sizeof(double));
+  cudaStream_t s = as_stream(stream);
+  double* partial = reinterpret_cast<double*>(workspace_dev);
+  entropy_rows_kernel<<<(unsigned)nctas, 256, 0, s>>>(p_dev, g, partial);
+  int st = check_launch("entropy_rows_kernel");
+  if (st) return st;
+  entropy_heads_kernel<<<(unsigned)((heads + 127) / 128), 128, 0, s>>>(partial, g, head_sums_dev);
+  return check_launch("entropy_heads_kernel");
+}

@@ -1,0 +1,494 @@
+// Row kernels: softmax (fused_softmax, kernels/pallas/fused_softmax.py:26-87) and LayerNorm
+// (fused_layernorm, kernels/pallas/fused_layernorm.py:26-119), forward and backward.
+//
+// HBM-bound single-pass design: one warp owns one row; the row is loaded once into registers
+// with 16-byte coalesced loads (consecutive lanes, consecutive 16-byte words), reduced with
+// warp shuffles and written once.  Statistics are fp32 whatever the storage dtype.  Rows too
+// long for registers use a three-sweep fallback that re-reads the row (served from L1/L2).
+#include "common.cuh"
+
+#include <algorithm>
+#include <math.h>
+
+XSAKE_DEFINE_DEVICE_ERROR(rowops)
+
+namespace xsake {
+namespace {
+
+// 16-byte vector of storage type T and its float expansion.
+template <typename T> struct Vec;
+template <> struct Vec<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const void* p, float* x) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  }
+  __device__ static void store(void* p, const float* x) {
+    *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+  }
+};
+template <> struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+  __device__ static void load(const void* p, float* x) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+      x[2 * i] = __bfloat162float(b.x);
+      x[2 * i + 1] = __bfloat162float(b.y);
+    }
+  }
+  __device__ static void store(void* p, const float* x) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 b = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+constexpr int kWarpsPerBlock = 8;
+
+// ---------------------------------------------------------------------------------- softmax
+template <typename T, int VPL>
+__global__ void __launch_bounds__(256) softmax_fwd_reg(const T* __restrict__ x, T* __restrict__ y,
+                                                       int64_t rows, int64_t cols) {
+  constexpr int N = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t nvec = cols / N;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    const T* xr = x + row * cols;
+    float v[VPL][N];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+        Vec<T>::load(xr + vi * N, v[k]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) v[k][i] = -INFINITY;
+      }
+#pragma unroll
+      for (int i = 0; i < N; ++i) mx = fmaxf(mx, v[k][i]);
+    }
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k)
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        v[k][i] = __expf(v[k][i] - mx);
+        sum += v[k][i];
+      }
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+    T* yr = y + row * cols;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) v[k][i] *= inv;
+        Vec<T>::store(yr + vi * N, v[k]);
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) softmax_fwd_generic(const T* __restrict__ x, T* __restrict__ y,
+                                                           int64_t rows, int64_t cols) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    const T* xr = x + row * cols;
+    float mx = -INFINITY;
+    for (int64_t c = lane; c < cols; c += 32) mx = fmaxf(mx, DT<T>::to_f(xr[c]));
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int64_t c = lane; c < cols; c += 32) sum += __expf(DT<T>::to_f(xr[c]) - mx);
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+    T* yr = y + row * cols;
+    for (int64_t c = lane; c < cols; c += 32) yr[c] = DT<T>::from_f(__expf(DT<T>::to_f(xr[c]) - mx) * inv);
+  }
+}
+
+template <typename T, int VPL>
+__global__ void __launch_bounds__(256) softmax_bwd_reg(const T* __restrict__ y, const T* __restrict__ dy,
+                                                       T* __restrict__ dx, int64_t rows, int64_t cols) {
+  constexpr int N = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t nvec = cols / N;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    float yv[VPL][N], gv[VPL][N];
+    float dot = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+        Vec<T>::load(y + row * cols + vi * N, yv[k]);
+        Vec<T>::load(dy + row * cols + vi * N, gv[k]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) yv[k][i] = gv[k][i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < N; ++i) dot = fmaf(yv[k][i], gv[k][i], dot);
+    }
+    dot = warp_sum(dot);
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+        float o[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) o[i] = yv[k][i] * (gv[k][i] - dot);
+        Vec<T>::store(dx + row * cols + vi * N, o);
+      }
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) softmax_bwd_generic(const T* __restrict__ y, const T* __restrict__ dy,
+                                                           T* __restrict__ dx, int64_t rows, int64_t cols) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    const int64_t o = row * cols;
+    float dot = 0.f;
+    for (int64_t c = lane; c < cols; c += 32) dot += DT<T>::to_f(y[o + c]) * DT<T>::to_f(dy[o + c]);
+    dot = warp_sum(dot);
+    for (int64_t c = lane; c < cols; c += 32)
+      dx[o + c] = DT<T>::from_f(DT<T>::to_f(y[o + c]) * (DT<T>::to_f(dy[o + c]) - dot));
+  }
+}
+
+// ---------------------------------------------------------------------------------- layernorm
+template <typename T, int VPL>
+__global__ void __launch_bounds__(256) layernorm_fwd_reg(const T* __restrict__ x, const float* __restrict__ gamma,
+                                                         const float* __restrict__ beta, float eps,
+                                                         T* __restrict__ y, float* __restrict__ mean_out,
+                                                         float* __restrict__ rstd_out, int64_t rows, int64_t d) {
+  constexpr int N = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const int64_t nvec = d / N;
+  float g[VPL][N], bt[VPL][N];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int64_t vi = lane + 32 * k;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      g[k][i] = vi < nvec ? gamma[vi * N + i] : 0.f;
+      bt[k][i] = vi < nvec ? beta[vi * N + i] : 0.f;
+    }
+  }
+  const float inv_d = 1.f / (float)d;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    const T* xr = x + row * d;
+    float v[VPL][N];
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+        Vec<T>::load(xr + vi * N, v[k]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) v[k][i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < N; ++i) s += v[k][i];
+    }
+    const float mean = warp_sum(s) * inv_d;
+    float q = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const float c = (vi < nvec) ? v[k][i] - mean : 0.f;
+        q = fmaf(c, c, q);
+      }
+    }
+    const float var = warp_sum(q) * inv_d;
+    const float rstd = 1.f / sqrtf(var + eps);
+    T* yr = y + row * d;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+        float o[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) o[i] = fmaf(g[k][i], (v[k][i] - mean) * rstd, bt[k][i]);
+        Vec<T>::store(yr + vi * N, o);
+      }
+    }
+    if (lane == 0) {
+      if (mean_out) mean_out[row] = mean;
+      if (rstd_out) rstd_out[row] = rstd;
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) layernorm_fwd_generic(const T* __restrict__ x, const float* __restrict__ gamma,
+                                                             const float* __restrict__ beta, float eps,
+                                                             T* __restrict__ y, float* __restrict__ mean_out,
+                                                             float* __restrict__ rstd_out, int64_t rows, int64_t d) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    const T* xr = x + row * d;
+    float s = 0.f;
+    for (int64_t c = lane; c < d; c += 32) s += DT<T>::to_f(xr[c]);
+    const float mean = warp_sum(s) / (float)d;
+    float q = 0.f;
+    for (int64_t c = lane; c < d; c += 32) {
+      const float t = DT<T>::to_f(xr[c]) - mean;
+      q = fmaf(t, t, q);
+    }
+    const float rstd = 1.f / sqrtf(warp_sum(q) / (float)d + eps);
+    for (int64_t c = lane; c < d; c += 32)
+      y[row * d + c] = DT<T>::from_f(fmaf(gamma[c], (DT<T>::to_f(xr[c]) - mean) * rstd, beta[c]));
+    if (lane == 0) {
+      if (mean_out) mean_out[row] = mean;
+      if (rstd_out) rstd_out[row] = rstd;
+    }
+  }
+}
+
+// dx = rstd * (g*dy - mean(g*dy) - xhat * mean(g*dy*xhat)); per-CTA partial column sums of
+// dy*xhat and dy go to `partial` [gridDim.x][2][d] and are reduced by ln_bwd_reduce.
+template <typename T>
+__global__ void __launch_bounds__(256) layernorm_bwd_rows(const T* __restrict__ x, const float* __restrict__ gamma,
+                                                          const float* __restrict__ mean_in,
+                                                          const float* __restrict__ rstd_in, const T* __restrict__ dy,
+                                                          T* __restrict__ dx, float* __restrict__ partial,
+                                                          int64_t rows, int64_t d) {
+  extern __shared__ float sacc[];  // [2][d]
+  for (int64_t c = threadIdx.x; c < 2 * d; c += blockDim.x) sacc[c] = 0.f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float inv_d = 1.f / (float)d;
+  // Rows are split into contiguous per-CTA ranges so the partial sums have a fixed order.
+  const int64_t per = (rows + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = (int64_t)blockIdx.x * per, r1 = min(rows, r0 + per);
+  for (int64_t row = r0 + warp; row < r1; row += kWarpsPerBlock) {
+    const int64_t o = row * d;
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float a1 = 0.f, a2 = 0.f;
+    for (int64_t c = lane; c < d; c += 32) {
+      const float xh = (DT<T>::to_f(x[o + c]) - mean) * rstd;
+      const float gd = gamma[c] * DT<T>::to_f(dy[o + c]);
+      a1 += gd;
+      a2 = fmaf(gd, xh, a2);
+    }
+    a1 = warp_sum(a1) * inv_d;
+    a2 = warp_sum(a2) * inv_d;
+    for (int64_t c = lane; c < d; c += 32) {
+      const float xh = (DT<T>::to_f(x[o + c]) - mean) * rstd;
+      const float g = DT<T>::to_f(dy[o + c]);
+      dx[o + c] = DT<T>::from_f(rstd * (gamma[c] * g - a1 - xh * a2));
+    }
+  }
+  // Column partials: warps take turns in a fixed order (deterministic).
+  for (int w = 0; w < kWarpsPerBlock; ++w) {
+    if (warp == w) {
+      for (int64_t row = r0 + warp; row < r1; row += kWarpsPerBlock) {
+        const int64_t o = row * d;
+        const float mean = mean_in[row], rstd = rstd_in[row];
+        for (int64_t c = lane; c < d; c += 32) {
+          const float g = DT<T>::to_f(dy[o + c]);
+          sacc[c] = fmaf(g, (DT<T>::to_f(x[o + c]) - mean) * rstd, sacc[c]);
+          sacc[d + c] += g;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  for (int64_t c = threadIdx.x; c < 2 * d; c += blockDim.x) partial[(int64_t)blockIdx.x * 2 * d + c] = sacc[c];
+}
+
+__global__ void ln_bwd_reduce(const float* __restrict__ partial, int nblocks, int64_t d, float* __restrict__ dgamma,
+                              float* __restrict__ dbeta) {
+  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= 2 * d) return;
+  float acc = 0.f;
+  for (int b = 0; b < nblocks; ++b) acc += partial[(int64_t)b * 2 * d + c];
+  if (c < d) dgamma[c] = acc; else dbeta[c - d] = acc;
+}
+
+int grid_for_rows(int64_t rows, int sm_count) {
+  const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sm_count * 32));
+}
+
+template <typename T>
+int softmax_fwd_t(int64_t rows, int64_t cols, const void* x, void* y, cudaStream_t s, int sms) {
+  constexpr int N = Vec<T>::N;
+  const T* xp = reinterpret_cast<const T*>(x);
+  T* yp = reinterpret_cast<T*>(y);
+  const int grid = grid_for_rows(rows, sms);
+  const bool vec_ok = cols % N == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0;
+  const int64_t per_lane = (cols / N + 31) / 32;
+  if (vec_ok && per_lane <= 1) softmax_fwd_reg<T, 1><<<grid, 256, 0, s>>>(xp, yp, rows, cols);
+  else if (vec_ok && per_lane <= 2) softmax_fwd_reg<T, 2><<<grid, 256, 0, s>>>(xp, yp, rows, cols);
+  else if (vec_ok && per_lane <= 4) softmax_fwd_reg<T, 4><<<grid, 256, 0, s>>>(xp, yp, rows, cols);
+  else if (vec_ok && per_lane <= 8) softmax_fwd_reg<T, 8><<<grid, 256, 0, s>>>(xp, yp, rows, cols);
+  else if (vec_ok && per_lane <= 16) softmax_fwd_reg<T, 16><<<grid, 256, 0, s>>>(xp, yp, rows, cols);
+  else softmax_fwd_generic<T><<<grid, 256, 0, s>>>(xp, yp, rows, cols);
+  return check_launch("softmax_fwd");
+}
+
+template <typename T>
+int softmax_bwd_t(int64_t rows, int64_t cols, const void* y, const void* dy, void* dx, cudaStream_t s, int sms) {
+  constexpr int N = Vec<T>::N;
+  const T* yp = reinterpret_cast<const T*>(y);
+  const T* gp = reinterpret_cast<const T*>(dy);
+  T* dp = reinterpret_cast<T*>(dx);
+  const int grid = grid_for_rows(rows, sms);
+  const bool vec_ok = cols % N == 0 && (((uintptr_t)y | (uintptr_t)dy | (uintptr_t)dx) & 15) == 0;
+  const int64_t per_lane = (cols / N + 31) / 32;
+  if (vec_ok && per_lane <= 2) softmax_bwd_reg<T, 2><<<grid, 256, 0, s>>>(yp, gp, dp, rows, cols);
+  else if (vec_ok && per_lane <= 4) softmax_bwd_reg<T, 4><<<grid, 256, 0, s>>>(yp, gp, dp, rows, cols);
+  else if (vec_ok && per_lane <= 8) softmax_bwd_reg<T, 8><<<grid, 256, 0, s>>>(yp, gp, dp, rows, cols);
+  else softmax_bwd_generic<T><<<grid, 256, 0, s>>>(yp, gp, dp, rows, cols);
+  return check_launch("softmax_bwd");
+}
+
+template <typename T>
+int layernorm_fwd_t(int64_t rows, int64_t d, const void* x, const float* g, const float* b, float eps, void* y,
+                    float* mean, float* rstd, cudaStream_t s, int sms) {
+  constexpr int N = Vec<T>::N;
+  const T* xp = reinterpret_cast<const T*>(x);
+  T* yp = reinterpret_cast<T*>(y);
+  const int grid = grid_for_rows(rows, sms);
+  const bool vec_ok = d % N == 0 && (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+  const int64_t per_lane = (d / N + 31) / 32;
+  if (vec_ok && per_lane <= 1) layernorm_fwd_reg<T, 1><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else if (vec_ok && per_lane <= 2) layernorm_fwd_reg<T, 2><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else if (vec_ok && per_lane <= 3) layernorm_fwd_reg<T, 3><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else if (vec_ok && per_lane <= 4) layernorm_fwd_reg<T, 4><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else if (vec_ok && per_lane <= 8) layernorm_fwd_reg<T, 8><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else layernorm_fwd_generic<T><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  return check_launch("layernorm_fwd");
+}
+
+int ln_bwd_blocks(int64_t rows, int sms) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((rows + 31) / 32, (int64_t)sms * 4));
+}
+
+}  // namespace
+}  // namespace xsake
+
+using namespace xsake;
+
+static int check_dtype(int32_t dt) {
+  XSAKE_REQUIRE(dt == XSAKE_F32 || dt == XSAKE_BF16, XSAKE_EINVAL, "dtype %d", dt);
+  return XSAKE_OK;
+}
+
+extern "C" int xsake_softmax_fwd(int32_t dtype, int64_t rows, int64_t cols, const void* x_dev, void* y_dev,
+                                 void* stream) {
+  clear_error();
+  int st = check_dtype(dtype);
+  if (st) return st;
+  XSAKE_REQUIRE(rows >= 0 && cols > 0, XSAKE_EINVAL, "rows must be >= 0 and cols > 0");
+  if (rows == 0) return XSAKE_OK;
+  XSAKE_REQUIRE(x_dev && y_dev, XSAKE_EINVAL, "NULL pointer");
+  DeviceInfo di;
+  if ((st = device_info(&di))) return st;
+  return dtype == XSAKE_F32 ? softmax_fwd_t<float>(rows, cols, x_dev, y_dev, as_stream(stream), di.sm_count)
+                            : softmax_fwd_t<__nv_bfloat16>(rows, cols, x_dev, y_dev, as_stream(stream), di.sm_count);
+}
+
+extern "C" int xsake_softmax_bwd(int32_t dtype, int64_t rows, int64_t cols, const void* y_dev, const void* dy_dev,
+                                 void* dx_dev, void* stream) {
+  clear_error();
+  int st = check_dtype(dtype);
+  if (st) return st;
+  XSAKE_REQUIRE(rows >= 0 && cols > 0, XSAKE_EINVAL, "rows must be >= 0 and cols > 0");
+  if (rows == 0) return XSAKE_OK;
+  XSAKE_REQUIRE(y_dev && dy_dev && dx_dev, XSAKE_EINVAL, "NULL pointer");
+  DeviceInfo di;
+  if ((st = device_info(&di))) return st;
+  return dtype == XSAKE_F32
+             ? softmax_bwd_t<float>(rows, cols, y_dev, dy_dev, dx_dev, as_stream(stream), di.sm_count)
+             : softmax_bwd_t<__nv_bfloat16>(rows, cols, y_dev, dy_dev, dx_dev, as_stream(stream), di.sm_count);
+}
+
+extern "C" int xsake_layernorm_fwd(int32_t x_dtype, int64_t rows, int64_t d, const void* x_dev,
+                                   const float* gamma_dev, const float* beta_dev, float eps, void* y_dev,
+                                   float* mean_dev, float* rstd_dev, void* stream) {
+  clear_error();
+  int st = check_dtype(x_dtype);
+  if (st) return st;
+  XSAKE_REQUIRE(rows >= 0 && d > 0, XSAKE_EINVAL, "rows must be >= 0 and d > 0");
+  XSAKE_REQUIRE(eps >= 0.f, XSAKE_EINVAL, "eps must be >= 0");
+  if (rows == 0) return XSAKE_OK;
+  XSAKE_REQUIRE(x_dev && gamma_dev && beta_dev && y_dev, XSAKE_EINVAL, "NULL pointer");
+  DeviceInfo di;
+  if ((st = device_info(&di))) return st;
+  cudaStream_t s = as_stream(stream);
+  return x_dtype == XSAKE_F32
+             ? layernorm_fwd_t<float>(rows, d, x_dev, gamma_dev, beta_dev, eps, y_dev, mean_dev, rstd_dev, s, di.sm_count)
+             : layernorm_fwd_t<__nv_bfloat16>(rows, d, x_dev, gamma_dev, beta_dev, eps, y_dev, mean_dev, rstd_dev, s,
+                                              di.sm_count);
+}
+
+extern "C" int xsake_layernorm_bwd_workspace_size(int64_t rows, int64_t d, size_t* bytes) {
+  clear_error();
+  XSAKE_REQUIRE(bytes != nullptr && rows >= 0 && d > 0, XSAKE_EINVAL, "bad arguments");
+  DeviceInfo di;
+  int st = device_info(&di);
+  const int sms = st ? 148 : di.sm_count;
+  clear_error();
+  *bytes = (size_t)ln_bwd_blocks(rows, sms) * 2 * (size_t)d * sizeof(float);
+  return XSAKE_OK;
+}
+
+extern "C" int xsake_layernorm_bwd(int32_t x_dtype, int64_t rows, int64_t d, const void* x_dev,
+                                   const float* gamma_dev, const float* mean_dev, const float* rstd_dev,
+                                   const void* dy_dev, void* dx_dev, float* dgamma_dev, float* dbeta_dev,
+                                   void* workspace_dev, size_t workspace_bytes, void* stream) {
+  clear_error();
+  int st = check_dtype(x_dtype);
+  if (st) return st;
+  XSAKE_REQUIRE(rows > 0 && d > 0, XSAKE_EINVAL, "rows and d must be positive");
+  XSAKE_REQUIRE(x_dev && gamma_dev && mean_dev && rstd_dev && dy_dev && dx_dev && dgamma_dev && dbeta_dev,
+                XSAKE_EINVAL, "NULL pointer");
+  XSAKE_REQUIRE(2 * d * sizeof(float) <= 96 * 1024, XSAKE_EUNSUPPORTED, "d too large for the backward");
+  DeviceInfo di;
+  if ((st = device_info(&di))) return st;
+  const int nb = ln_bwd_blocks(rows, di.sm_count);
+  XSAKE_REQUIRE(workspace_dev && workspace_bytes >= (size_t)nb * 2 * d * sizeof(float), XSAKE_EINVAL,
+                "workspace too small");
+  cudaStream_t s = as_stream(stream);
+  const size_t smem = 2 * d * sizeof(float);
+  float* partial = reinterpret_cast<float*>(workspace_dev);
+  if (x_dtype == XSAKE_F32) {
+    if (smem > 48 * 1024)
+      XSAKE_CUDA_TRY(cudaFuncSetAttribute(layernorm_bwd_rows<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    layernorm_bwd_rows<float><<<nb, 256, smem, s>>>((const float*)x_dev, gamma_dev, mean_dev, rstd_dev,
+                                                    (const float*)dy_dev, (float*)dx_dev, partial, rows, d);
+  } else {
+    if (smem > 48 * 1024)
+      XSAKE_CUDA_TRY(cudaFuncSetAttribute(layernorm_bwd_rows<__nv_bfloat16>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    layernorm_bwd_rows<__nv_bfloat16><<<nb, 256, smem, s>>>(
+        (const __nv_bfloat16*)x_dev, gamma_dev, mean_dev, rstd_dev, (const __nv_bfloat16*)dy_dev,
+        (__nv_bfloat16*)dx_dev, partial, rows, d);
+  }
+  if ((st = check_launch("layernorm_bwd_rows"))) return st;
+  ln_bwd_reduce<<<(int)((2 * d + 255) / 256), 256, 0, s>>>(partial, nb, d, dgamma_dev, dbeta_dev);
+  return check_launch("ln_bwd_reduce");
+}
