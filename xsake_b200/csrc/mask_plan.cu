@@ -180,7 +180,7 @@ __global__ void plan_scan_kernel(PlanLayout L, int32_t* __restrict__ plan) {
         for (int i = 0; i < L.nitems; ++i) {
           const int t = i % L.npairs, bh = i / L.npairs;
           const int r = L.group_of(bh / L.H, bh % L.H) * L.npairs + t;
-          tiles += rp[r + 1] - rp[r];
+          tiles += 2 * (rp[r + 1] - rp[r]);   // each entry is a 128x64 tile = two 64x64 tiles
         }
       }
       const int64_t active = (int64_t)s_active * mult_b * mult_h;
