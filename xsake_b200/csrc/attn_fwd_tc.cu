@@ -255,7 +255,10 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const int r = L.group_of(b, h) * L.npairs + t;
         const int e0 = rowptr[r], n = rowptr[r + 1] - e0;
         float m = -INFINITY, l = 0.f;
+        int32_t e_next = n > 0 ? entries[e0] : 0;
         for (int i = 0; i < n; ++i, ++it) {
+          const int32_t e = e_next;
+          if (i + 1 < n) e_next = entries[e0 + i + 1];   // prefetch: off the critical path
           const uint32_t sb = it & 1;
           if (!warp_mbar_wait(&bars->s_full[sb], (it >> 1) & 1, abort)) { ok = false; break; }
           tc_fence_after();
@@ -266,19 +269,26 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
           XSAKE_TMEM_WAIT_LD32((sr + 32));
           tc_fence_before();
           mbar_arrive(&bars->s_free[sb]);
-          const int32_t e = entries[e0 + i];
           bool waited = false;
           uint32_t pk[32];
           if (e & f_active) {
-            float* x = reinterpret_cast<float*>(sr);   // scores, scaled in place (log2 units)
-            float mx = -INFINITY;
-            const bool diag = (e & f_diag) != 0;
+            float* x = reinterpret_cast<float*>(sr);   // raw scores
+            if (e & f_diag) {                          // warp-uniform: token-level causal cut
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
-              x[j] = __uint_as_float(sr[j]) * p.scale_log2;
-              if (diag && j > diag_lim) x[j] = -INFINITY;
-              mx = fmaxf(mx, x[j]);
+              for (int j = 0; j < 64; ++j)
+                if (j > diag_lim) x[j] = -INFINITY;
             }
+            // Row max of the raw scores: a depth-4 tree of 3-input maxes.
+            float t1[22];
+#pragma unroll
+            for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+            t1[21] = x[63];
+            float t2[8];
+#pragma unroll
+            for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
+            t2[7] = t1[21];
+            const float mraw = fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
+            const float mx = mraw * p.scale_log2;       // log2 units (scale > 0)
             const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
             if (m == -INFINITY) m = mx;
             // TMEM loads/stores are warp-collective: the whole warp rescales when any row must.
@@ -303,16 +313,28 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 m = mx;
               }
             }
-            float ls = 0.f;
             const float msub = (m == -INFINITY) ? 0.f : m;   // no live score yet: every x is -inf
+            // p = 2^(s*scale*log2e - m): one packed FMA per pair; 3 of every 8 pairs go through
+            // the polynomial exp2 on the FMA/ALU pipes, the rest through MUFU ex2.
+            const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
+            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float p0 = ex2(x[2 * j] - msub), p1 = ex2(x[2 * j + 1] - msub);
-              ls += p0 + p1;
+              float x0, x1, p0, p1;
+              upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
+              if ((j & 7) < 3) {
+                exp2_poly2(x0, x1, p0, p1);
+              } else {
+                p0 = ex2(x0);
+                p1 = ex2(x1);
+              }
+              acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
               __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
               pk[j] = *reinterpret_cast<uint32_t*>(&pb);
             }
-            l += ls;
+            float s0, s1;
+            upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
+            l += s0 + s1;
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j) pk[j] = 0u;

@@ -8,7 +8,7 @@
 #include <stdarg.h>
 #include <string>
 
-#include "../../include/xsake_hads.h"
+#include "xsake_hads.h"
 
 namespace xsake {
 
