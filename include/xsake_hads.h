@@ -142,6 +142,18 @@ XSAKE_API int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t head
                        int64_t sk, double* head_sums_dev, void* workspace_dev,
                        size_t workspace_bytes, void* stream);
 
+/* Same result as xsake_entropy_rows for callers that can neither pass a workspace nor allocate
+ * device memory (a framework plugin that may only use its framework's allocator, a process
+ * whose device memory is all held by a pool allocator, a loop that cannot afford cudaMalloc's
+ * device synchronisation).  It has no counterpart in the reference: the reference never
+ * manages device memory itself.  Scratch is a library-owned static device array of 65,536
+ * fp64 partial sums (512 KiB on every GPU that loads the library): calls needing more
+ * (batch * heads * ctas_per_slice, ctas_per_slice = seq_q / largest divisor of seq_q <= 64)
+ * return XSAKE_EUNSUPPORTED.  The first call on a device resolves the array's address; make it
+ * before any stream capture.  All calls share the array, so calls overlapping on the GPU race. */
+XSAKE_API int xsake_entropy_rows_noalloc(const float* p_dev, int64_t batch, int64_t heads,
+                       int64_t sq, int64_t sk, double* head_sums_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

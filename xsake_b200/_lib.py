@@ -61,6 +61,7 @@ _SIGS = {
                                       _VP, _SZ, _VP]),
     "xsake_entropy_workspace_size": (C.c_int, [_I64, _I64, _I64, C.POINTER(_SZ)]),
     "xsake_entropy_rows": (C.c_int, [_VP, _I64, _I64, _I64, _I64, _VP, _VP, _SZ, _VP]),
+    "xsake_entropy_rows_noalloc": (C.c_int, [_VP, _I64, _I64, _I64, _I64, _VP, _VP]),
 }
 
 _lib = None

@@ -7,6 +7,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 XSAKE_DEFINE_DEVICE_ERROR(entropy)
 
@@ -118,6 +119,77 @@ extern "C" int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t hea
   entropy_rows_kernel<<<(unsigned)nctas, 256, 0, s>>>(p_dev, g, partial);
   int st = check_launch("entropy_rows_kernel");
   if (st) return st;
+  entropy_heads_kernel<<<(unsigned)((heads + 127) / 128), 128, 0, s>>>(partial, g, head_sums_dev);
+  return check_launch("entropy_heads_kernel");
+}
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant of xsake_entropy_rows.
+//
+// Some callers cannot hand this library a device workspace and cannot allocate one either:
+// a framework plugin (for example an XLA FFI handler) must take every byte of device memory
+// from its framework's allocator, and a process whose memory is fully reserved by a pool
+// allocator would see a raw cudaMalloc fail; cudaMalloc also synchronises the device, which
+// a latency-critical loop cannot afford.  For them the per-CTA partial sums live in the
+// static device array below instead of a workspace.
+//
+// Limits and behaviour:
+//   * at most kNoAllocMaxPartials = 65,536 partial sums (512 KiB, held by every GPU that loads
+//     the library until the process exits): batch * heads * ctas_per_slice must not exceed it,
+//     where ctas_per_slice = seq_q / (largest divisor of seq_q that is <= 64); larger calls are
+//     rejected with XSAKE_EUNSUPPORTED before anything is launched;
+//   * the first call on each device looks up the array's device address with
+//     cudaGetSymbolAddress (with that device current); make that first call before any stream
+//     capture begins;
+//   * all calls share the one array: calls that overlap on the GPU (concurrent streams) race
+//     and corrupt each other's results; calls ordered on one stream are fine;
+//   * the array keeps the previous call's contents; nothing needs clearing because every slot a
+//     call reads is first written by the same call.
+namespace xsake {
+namespace {
+
+constexpr int64_t kNoAllocMaxPartials = 65536;
+static __device__ __align__(256) double g_entropy_partials[kNoAllocMaxPartials];
+
+constexpr int kNoAllocMaxDevices = 64;
+double* g_partials_ptr[kNoAllocMaxDevices];
+cudaError_t g_partials_err[kNoAllocMaxDevices];
+std::once_flag g_partials_once[kNoAllocMaxDevices];
+
+int partials_address(double** out) {
+  int dev = 0;
+  XSAKE_CUDA_TRY(cudaGetDevice(&dev));
+  XSAKE_REQUIRE(dev >= 0 && dev < kNoAllocMaxDevices, XSAKE_EUNSUPPORTED, "device ordinal %d", dev);
+  std::call_once(g_partials_once[dev], [dev] {
+    g_partials_err[dev] = cudaGetSymbolAddress(reinterpret_cast<void**>(&g_partials_ptr[dev]), g_entropy_partials);
+  });
+  XSAKE_REQUIRE(g_partials_err[dev] == cudaSuccess, XSAKE_ECUDA, "cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(g_partials_err[dev]));
+  *out = g_partials_ptr[dev];
+  return XSAKE_OK;
+}
+
+}  // namespace
+}  // namespace xsake
+
+extern "C" int xsake_entropy_rows_noalloc(const float* p_dev, int64_t batch, int64_t heads, int64_t sq, int64_t sk,
+                                          double* head_sums_dev, void* stream) {
+  clear_error();
+  XSAKE_REQUIRE(batch > 0 && heads > 0 && sq > 0 && sk > 0, XSAKE_EINVAL, "dims must be positive");
+  XSAKE_REQUIRE(p_dev && head_sums_dev, XSAKE_EINVAL, "NULL pointer");
+  XSAKE_REQUIRE(((uintptr_t)p_dev & 15) == 0, XSAKE_EINVAL, "p must be 16-byte aligned");
+  const EntropyGeom g = geom(batch, heads, sq, sk);
+  const int64_t nctas = batch * heads * g.ctas_per_bh;
+  XSAKE_REQUIRE(nctas <= kNoAllocMaxPartials, XSAKE_EUNSUPPORTED,
+                "xsake_entropy_rows_noalloc: %lld partial sums exceed its static limit of %lld "
+                "(batch * heads * ctas_per_slice); use xsake_entropy_rows with a workspace",
+                (long long)nctas, (long long)kNoAllocMaxPartials);
+  double* partial = nullptr;
+  int st = partials_address(&partial);
+  if (st) return st;
+  cudaStream_t s = as_stream(stream);
+  entropy_rows_kernel<<<(unsigned)nctas, 256, 0, s>>>(p_dev, g, partial);
+  if ((st = check_launch("entropy_rows_kernel"))) return st;
   entropy_heads_kernel<<<(unsigned)((heads + 127) / 128), 128, 0, s>>>(partial, g, head_sums_dev);
   return check_launch("entropy_heads_kernel");
 }
