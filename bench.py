@@ -246,13 +246,16 @@ def run_attention(args, dist, rank, world, local):
         sets.append((q, k, v, o, lse))
     lib = _lib.load()
     desc = sa._desc(sets[0][0], sets[0][1], sets[0][2], sets[0][3], cm, None)
+    ws_n = C.c_size_t(0)
+    _lib.check(lib.xsake_attn_fwd_workspace_size(C.byref(desc), C.byref(ws_n)))
+    ws = torch.empty(max(ws_n.value, 16), dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
     def step(i):
         q, k, v, o, lse = sets[i % nsets]
         st = lib.xsake_attn_fwd(C.byref(desc), cm.plan.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                o.data_ptr(), lse.data_ptr(), None, 0, sp)
+                                o.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), sp)
         if st:
             _lib.check(st)
 

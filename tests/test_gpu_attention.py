@@ -215,7 +215,8 @@ def test_plan_mismatch_is_reported_not_faulted():
     lib = _lib.load()
     stream = sa.dev.stream_ptr()
     _lib.device_error(stream)                            # clear earlier words
+    ws = torch.zeros(256, dtype=torch.uint8, device="cuda")
     _lib.check(lib.xsake_attn_fwd(C.byref(d), cm.plan.data_ptr(), q.data_ptr(), q.data_ptr(),
-                                  q.data_ptr(), o.data_ptr(), lse.data_ptr(), None, 0, stream))
+                                  q.data_ptr(), o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, stream))
     code = _lib.device_error(stream)
     assert code >> 24 == 2

@@ -50,7 +50,7 @@ using namespace xsake;
 extern "C" int xsake_attn_fwd_workspace_size(const XsakeAttnDesc* desc, size_t* bytes) {
   clear_error();
   XSAKE_REQUIRE(desc && bytes, XSAKE_EINVAL, "NULL argument");
-  *bytes = 0;
+  *bytes = 256;   // work-item counter of the persistent tensor-core kernel
   return XSAKE_OK;
 }
 

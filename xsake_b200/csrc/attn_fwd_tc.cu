@@ -8,17 +8,25 @@
 // (the Pallas kernel ignores `causal`, the reference CPU path applies it, :79-81), and lse is
 // returned.
 //
-// Work item = 128 query rows (two 64-row chunks 2t, 2t+1 of one (b, h)) and the union of their
-// active 64-key chunks.  Per chunk: S = Q K^T (tcgen05, M=128 N=64 K=64, fp32 in TMEM),
-// softmax by one thread per row straight out of TMEM, P (bf16) to shared memory, O += P V
-// (tcgen05, fp32 accumulator resident in TMEM).  Roles per CTA (192 threads):
-//   warps 0-3  softmax + epilogue, thread i owns row i (TMEM lane i)
-//   warp 4     TMA producer: Q tile once per item, K/V chunks into a 4-stage ring
-//   warp 5     MMA issuer (one thread): QK of chunk i+1 is queued before PV of chunk i
-// Two CTAs per SM (97 KB smem, 256 TMEM columns each) so one CTA's softmax overlaps the
-// other's MMAs.  The running max is only moved when it grows by more than 2^8 (rescaling O in
-// TMEM is then rare); exp2 runs on the MUFU unit.  Items are taken in descending-cost order
-// with a boustrophedon assignment over the persistent CTAs.
+// Work item = 256 query rows of one (b, h): tile A = 64-row chunks (4u, 4u+1), tile B =
+// (4u+2, 4u+3).  The item walks the merged, ascending list of 64-key chunks either tile
+// attends; each chunk's K/V tile is loaded once (TMA, SWIZZLE_128B) into an 8-stage ring and
+// used by both tiles when both attend it.  Per tile and chunk: S = Q K^T (tcgen05, M=128 N=64
+// K=64, fp32 in TMEM), softmax by one thread per query row straight out of TMEM, P (bf16) to
+// shared memory, O += P V (tcgen05, fp32 accumulator resident in TMEM).
+// Roles (352 threads, one CTA per SM, persistent):
+//   warps 0-3  softmax + epilogue of tile A (thread i owns row i = TMEM lane i)
+//   warps 4-7  softmax + epilogue of tile B
+//   warp 8     scheduler + TMA producer: takes items from a global counter (longest first),
+//              publishes them through a 2-slot ring, loads Q (double-buffered) and K/V
+//   warps 9,10 MMA issuers of tiles A and B (one elected lane each): QK of a tile's chunk i
+//              is queued before its PV of chunk i-1; a ring stage is released once both
+//              warps are done with it
+// TMEM: 512 columns; per tile (at 256*tile) three S buffers [0,64) [64,128) [128,192) so QK
+// runs two chunks ahead of the softmax, and O at [192,256).  P is double-buffered in shared
+// memory, so the softmax of chunk s only needs the PV of chunk s-2 to have finished.
+// The running max is only moved when it grows by more than 2^8 (rescaling O in TMEM is then
+// rare); exp2 runs on MUFU for 5/8 of the elements and on a cubic polynomial for the rest.
 #include "attn_common.cuh"
 #include "sm100.cuh"
 
@@ -33,39 +41,39 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kStages = 6;
+constexpr int kThreads = 352;
 constexpr int kQBytes = 128 * 64 * 2;
 constexpr int kKBytes = 64 * 64 * 2;
 constexpr int kStageBytes = 2 * kKBytes;
-constexpr int kOffQ = 0;
-constexpr int kOffKV = kOffQ + kQBytes;
-constexpr int kOffP = kOffKV + kStages * kStageBytes;
-constexpr int kOffBar = kOffP + kQBytes;
-constexpr int kNumBars = 2 + 2 * kStages + 2 + 2 + 4;
-constexpr int kOffMisc = kOffBar + kNumBars * 8;
-constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
-constexpr uint32_t kTmemCols = 256;               // S0 [0,64) S1 [64,128) O [128,192)
-constexpr uint32_t kIdescQK = idesc_bf16(128, 64, false);
-constexpr uint32_t kIdescPV = idesc_bf16(128, 64, true);
-constexpr float kRescaleThreshold = 8.0f;          // log2 units
+constexpr int kOffQ = 0;                              // [2 slots][2 tiles]
+constexpr int kOffP = kOffQ + 4 * kQBytes;            // [2 tiles][2 buffers]
+constexpr int kOffKV = kOffP + 4 * kQBytes;           // [kStages] K then V
+constexpr int kOffBar = kOffKV + kStages * kStageBytes;
 
 struct Bars {
-  uint64_t q_full, q_empty;
+  uint64_t item_full[2], item_empty[2];
+  uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kStages], kv_empty[kStages];
-  uint64_t s_full[2], s_free[2];
-  uint64_t p_full, o_done, o_free, drain;
+  uint64_t s_full[2][3];                 // [tile][S buffer]
+  uint64_t p_full[2][2], o_done[2][2];   // [tile][P buffer]
+  uint64_t o_free[2];
+  uint64_t drain;
 };
-static_assert(sizeof(Bars) == kNumBars * 8, "barrier block size");
+constexpr int kOffMisc = kOffBar + (int)sizeof(Bars);
+constexpr int kSmemBytes = kOffMisc + 64 + 1024;      // + alignment slack
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kIdescQK = idesc_bf16(128, 64, false);
+constexpr uint32_t kIdescPV = idesc_bf16(128, 64, true);
+constexpr float kRescaleThreshold = 8.0f;             // log2 units
+constexpr int kItemReaders = 2 + 256;                 // both MMA warps + both softmax warpgroups
 
 struct TcParams {
   AttnArgs a;
   float scale_log2;
+  int* counter;   // zeroed by the host before the launch
 };
-
-__device__ __forceinline__ int snake_rank(int round, int cta, int G) {
-  return round * G + ((round & 1) ? (G - 1 - cta) : cta);
-}
 
 __device__ __forceinline__ void fail(volatile int* abort, int detail) {
   if (atomicExch((int*)abort, 1) == 0) record_device_error(DEV_ERR_TIMEOUT, detail);
@@ -84,7 +92,24 @@ __device__ void warp_mean_v(const AttnArgs& a, int b, int h, float2& mine) {
   mine = make_float2(s0 / a.S, s1 / a.S);
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+struct Item {
+  int b, h, u, e0, n;
+};
+
+__device__ __forceinline__ Item decode(const AttnArgs& a, const int32_t* rowptr, int item) {
+  const PlanLayout& L = a.L;
+  Item it;
+  it.u = item % L.nquads;
+  const int bh = item / L.nquads;
+  it.b = bh / a.H;
+  it.h = bh % a.H;
+  const int r = L.group_of(it.b, it.h) * L.nquads + it.u;
+  it.e0 = rowptr[r];
+  it.n = rowptr[r + 1] - it.e0;
+  return it;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
 tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
               const __grid_constant__ CUtensorMap tmV, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -93,31 +118,36 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
   volatile int* plan_ok = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
+  volatile int* item_slot = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);   // [2]
   const AttnArgs& a = p.a;
+  const PlanLayout& L = a.L;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     *abort = 0;
     *plan_ok = plan_matches(a) && a.plan[H_HAS_CSR] == 1;
     if (!*plan_ok) record_device_error(DEV_ERR_PLAN, 10);
-    mbar_init(&bars->q_full, 1);
-    mbar_init(&bars->q_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->item_full[s], 1);
+      mbar_init(&bars->item_empty[s], kItemReaders);
+      mbar_init(&bars->q_full[s], 1);
+      mbar_init(&bars->q_empty[s], 2);        // one release per tile's MMA warp
+      mbar_init(&bars->o_free[s], 128);
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(&bars->p_full[s][b], 128);
+        mbar_init(&bars->o_done[s][b], 1);
+      }
+      for (int b = 0; b < 3; ++b) mbar_init(&bars->s_full[s][b], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->kv_empty[s], 2);       // one release per tile's MMA warp
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars->s_full[s], 1);
-      mbar_init(&bars->s_free[s], 128);
-    }
-    mbar_init(&bars->p_full, 128);
-    mbar_init(&bars->o_done, 1);
-    mbar_init(&bars->o_free, 128);
-    mbar_init(&bars->drain, 1);
+    mbar_init(&bars->drain, 2);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&tmQ);
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
@@ -130,146 +160,218 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  const PlanLayout& L = a.L;
-  const int32_t* rowptr = a.plan + L.f_rowptr_off;
-  const int32_t* entries = a.plan + L.f_entries_off;
-  const int32_t* items = a.plan + L.f_items_off;
-  const int G = gridDim.x, cta = blockIdx.x;
+  const int32_t* rowptr = a.plan + L.q_rowptr_off;
+  const int32_t* entries = a.plan + L.q_entries_off;
+  const int32_t* items = a.plan + L.q_items_off;
 
   if (*plan_ok) {
-    if (warp == 4) {
-      // ------------------------------------------------------------------ TMA producer
-      if (lane == 0) {
-        uint32_t it = 0, jj = 0;
-        for (int round = 0;; ++round) {
-          const int rank = snake_rank(round, cta, G);
-          if (rank >= L.nitems || *abort) break;
-          const int item = items[rank];
-          const int t = item % L.npairs, bh = item / L.npairs, b = bh / a.H, h = bh % a.H;
-          const int r = L.group_of(b, h) * L.npairs + t;
-          const int e0 = rowptr[r], n = rowptr[r + 1] - e0;
-          if (n == 0) continue;
-          if (!mbar_wait(&bars->q_empty, (jj & 1) ^ 1, abort)) { fail(abort, 1); break; }
-          mbar_arrive_expect_tx(&bars->q_full, kQBytes);
-          tma_load_4d(smem + kOffQ, &tmQ, &bars->q_full, 0, 128 * t, h, b);
-          bool ok = true;
-          for (int i = 0; i < n; ++i, ++it) {
-            const int st = it % kStages;
-            if (!mbar_wait(&bars->kv_empty[st], ((it / kStages) & 1) ^ 1, abort)) { ok = false; break; }
-            const int c = entries[e0 + i] & kEntryIdxMask;
+    if (warp == 8) {
+      // ------------------------------------------------------------------ scheduler + TMA
+      // The whole warp runs the (uniform) control flow; one elected lane issues.
+      uint32_t it = 0, qk = 0;
+      bool ok = true;
+      for (uint32_t k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!warp_mbar_wait(&bars->item_empty[slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+        int idx = 0;
+        if (lane == 0) idx = *abort ? L.nqitems : atomicAdd(p.counter, 1);
+        idx = __shfl_sync(0xffffffffu, idx, 0);
+        const int item = idx < L.nqitems ? items[idx] : -1;
+        if (elect_one()) {
+          item_slot[slot] = item;
+          mbar_arrive(&bars->item_full[slot]);
+        }
+        __syncwarp();
+        if (item < 0) break;
+        const Item w = decode(a, rowptr, item);
+        if (w.n == 0) continue;
+        const int qs = qk & 1;
+        if (!warp_mbar_wait(&bars->q_empty[qs], ((qk >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+        const int row0 = 256 * w.u;
+        const bool has_b = row0 + 128 < a.S;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&bars->q_full[qs], has_b ? 2 * kQBytes : kQBytes);
+          tma_load_4d(smem + kOffQ + (2 * qs) * kQBytes, &tmQ, &bars->q_full[qs], 0, row0, w.h, w.b);
+          if (has_b)
+            tma_load_4d(smem + kOffQ + (2 * qs + 1) * kQBytes, &tmQ, &bars->q_full[qs], 0, row0 + 128, w.h, w.b);
+        }
+        __syncwarp();
+        ++qk;
+        int32_t e_next = entries[w.e0];
+        for (int i = 0; i < w.n; ++i, ++it) {
+          const int c = e_next & kEntryIdxMask;
+          if (i + 1 < w.n) e_next = entries[w.e0 + i + 1];
+          const int st = it % kStages;
+          if (!warp_mbar_wait(&bars->kv_empty[st], ((it / kStages) & 1) ^ 1, abort)) { ok = false; break; }
+          if (elect_one()) {
             uint8_t* kbuf = smem + kOffKV + st * kStageBytes;
             mbar_arrive_expect_tx(&bars->kv_full[st], kStageBytes);
-            tma_load_4d(kbuf, &tmK, &bars->kv_full[st], 0, 64 * c, h, b);
-            tma_load_4d(kbuf + kKBytes, &tmV, &bars->kv_full[st], 0, 64 * c, h, b);
+            tma_load_4d(kbuf, &tmK, &bars->kv_full[st], 0, 64 * c, w.h, w.b);
+            tma_load_4d(kbuf + kKBytes, &tmV, &bars->kv_full[st], 0, 64 * c, w.h, w.b);
           }
-          if (!ok) { fail(abort, 2); break; }
-          ++jj;
+          __syncwarp();
         }
-        // Every load issued above has been consumed by the MMA warp on the normal path; on
-        // the abort path give in-flight copies a bounded chance to land before exit.
-        if (*abort) {
-          for (int s = 0; s < kStages; ++s) {
-            const uint64_t t0 = global_timer_ns();
-            while (!mbar_try_wait(&bars->kv_full[s], 0) && !mbar_try_wait(&bars->kv_full[s], 1) &&
-                   global_timer_ns() - t0 < 1000000ull) {
-            }
+      }
+      if (!ok && lane == 0) {
+        fail(abort, 1);
+        // Give copies in flight a bounded chance to land before the CTA exits.
+        for (int s = 0; s < kStages; ++s) {
+          const uint64_t t0 = global_timer_ns();
+          while (!mbar_try_wait(&bars->kv_full[s], 0) && !mbar_try_wait(&bars->kv_full[s], 1) &&
+                 global_timer_ns() - t0 < 1000000ull) {
           }
         }
       }
-    } else if (warp == 5) {
-      // ------------------------------------------------------------------ MMA issuer
-      if (lane == 0) {
-        const uint32_t q_addr = smem_u32(smem + kOffQ);
-        const uint32_t p_addr = smem_u32(smem + kOffP);
-        const uint64_t qdesc = sw128_desc(q_addr, 16, 1024);
-        const uint64_t pdesc = sw128_desc(p_addr, 16, 1024);
-        uint32_t it = 0, jj = 0;
-        bool ok = true;
-        auto issue_pv = [&](uint32_t x, bool first) -> bool {
-          if (!mbar_wait(&bars->p_full, x & 1, abort)) return false;
-          if (first && jj > 0 && !mbar_wait(&bars->o_free, (jj - 1) & 1, abort)) return false;
-          tc_fence_after();
-          const int st = x % kStages;
-          const uint32_t v_addr = smem_u32(smem + kOffKV + st * kStageBytes + kKBytes);
-          const uint64_t vdesc = sw128_desc(v_addr, 16, 1024);
+    } else if (warp == 9 || warp == 10) {
+      // ------------------------------------------------------------------ MMA issuers
+      // One warp per tile (X = warp - 9), so the two tiles' MMA streams issue independently.
+      // The whole warp runs the (uniform) control flow; one elected lane issues.  Every entry
+      // of the merged list is visited in order: an entry this tile does not use is released to
+      // the producer at once (after its load landed, so the release cannot run ahead of the
+      // ring).  QK of step s goes into S buffer s%3 once PV(s-3) has been issued (which implies
+      // the softmax has read S(s-3)); PV(s-2) is issued right after QK(s).
+      const int X = warp - 9;
+      const int32_t f_tile = kQuadFlagsA << (kQuadShiftB * X);
+      const uint32_t tcol = tmem + 256 * X;
+      const uint64_t pdesc0 = sw128_desc(smem_u32(smem + kOffP + (2 * X) * kQBytes), 16, 1024);
+      const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV), 16, 1024);
+      uint32_t it = 0, qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
+      int pstage[3] = {0, 0, 0};
+      bool ok = true;
+      auto issue_pv = [&]() -> bool {
+        const uint32_t s = pvs, pb = s & 1;
+        if (!warp_mbar_wait(&bars->p_full[X][pb], (s >> 1) & 1, abort)) return false;
+        const bool first = (s == item_first);
+        if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
+        tc_fence_after();
+        const int st = pstage[s % 3];
+        if (elect_one()) {
+          const uint64_t pdesc = pdesc0 + (uint64_t)((pb * kQBytes) >> 4);
+          const uint64_t vdesc = kdesc0 + (uint64_t)((st * kStageBytes + kKBytes) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_bf16_ss(tmem + 128, pdesc + 2 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
+            mma_bf16_ss(tcol + 192, pdesc + 2 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
                         (first && kk == 0) ? 0u : 1u);
-          mma_commit(&bars->o_done);
+          mma_commit(&bars->o_done[X][pb]);
           mma_commit(&bars->kv_empty[st]);
-          return true;
-        };
-        for (int round = 0; ok; ++round) {
-          const int rank = snake_rank(round, cta, G);
-          if (rank >= L.nitems || *abort) break;
-          const int item = items[rank];
-          const int t = item % L.npairs, bh = item / L.npairs;
-          const int r = L.group_of(bh / a.H, bh % a.H) * L.npairs + t;
-          const int n = rowptr[r + 1] - rowptr[r];
-          if (n == 0) continue;
-          if (!mbar_wait(&bars->q_full, jj & 1, abort)) { ok = false; break; }
-          for (int i = 0; i < n && ok; ++i, ++it) {
-            const int st = it % kStages;
-            const uint32_t sb = it & 1;
-            if (!mbar_wait(&bars->kv_full[st], (it / kStages) & 1, abort) ||
-                !mbar_wait(&bars->s_free[sb], ((it >> 1) & 1) ^ 1, abort)) { ok = false; break; }
-            tc_fence_after();
-            const uint64_t kdesc = sw128_desc(smem_u32(smem + kOffKV + st * kStageBytes), 16, 1024);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_ss(tmem + 64 * sb, qdesc + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
-            mma_commit(&bars->s_full[sb]);
-            if (i == n - 1) mma_commit(&bars->q_empty);
-            if (i > 0 && !issue_pv(it - 1, i == 1)) { ok = false; break; }
-          }
-          if (!ok) break;
-          if (!issue_pv(it - 1, n == 1)) { ok = false; break; }
-          ++jj;
         }
-        if (!ok) fail(abort, 3);
-        // Drain: no MMA may be in flight when TMEM is released.
-        mma_commit(&bars->drain);
+        __syncwarp();
+        ++pvs;
+        return true;
+      };
+      for (uint32_t k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!warp_mbar_wait(&bars->item_full[slot], (k >> 1) & 1, abort)) { ok = false; break; }
+        const int item = item_slot[slot];
+        __syncwarp();
+        if (elect_one()) mbar_arrive(&bars->item_empty[slot]);
+        __syncwarp();
+        if (item < 0) break;
+        const Item w = decode(a, rowptr, item);
+        if (w.n == 0) continue;
+        const int qs = qk & 1;
+        if (!warp_mbar_wait(&bars->q_full[qs], (qk >> 1) & 1, abort)) { ok = false; break; }
+        ++qk;
+        const uint64_t qdesc = sw128_desc(smem_u32(smem + kOffQ + (2 * qs + X) * kQBytes), 16, 1024);
+        item_first = steps;
+        int last_used = -1;
+        for (int i = 0; i < w.n; ++i)
+          if (entries[w.e0 + i] & f_tile) last_used = i;
+        int32_t e_next = entries[w.e0];
+        for (int i = 0; i < w.n && ok; ++i, ++it) {
+          const int32_t e = e_next;
+          if (i + 1 < w.n) e_next = entries[w.e0 + i + 1];
+          const int st = it % kStages;
+          // Pending PVs hold ring stages: before skipping over an entry this tile does not use,
+          // issue them all, or a long run of the other tile's entries could wait on those stages.
+          if (!(e & f_tile))
+            while (ok && pvs < steps) ok = issue_pv();
+          if (!ok) break;
+          if (!warp_mbar_wait(&bars->kv_full[st], (it / kStages) & 1, abort)) { ok = false; break; }
+          if (e & f_tile) {
+            while (ok && pvs + 3 <= steps) ok = issue_pv();   // S buffer steps%3 must be free
+            if (!ok) break;
+            const uint32_t sb = steps % 3;
+            tc_fence_after();
+            if (elect_one()) {
+              const uint64_t kdesc = kdesc0 + (uint64_t)((st * kStageBytes) >> 4);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_bf16_ss(tcol + 64 * sb, qdesc + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
+              mma_commit(&bars->s_full[X][sb]);
+              if (i == last_used) mma_commit(&bars->q_empty[qs]);
+            }
+            __syncwarp();
+            pstage[sb] = st;
+            ++steps;
+            if (pvs + 2 < steps && !issue_pv()) { ok = false; break; }   // keep PV two steps behind
+          } else {
+            if (elect_one()) mbar_arrive(&bars->kv_empty[st]);
+            __syncwarp();
+          }
+        }
+        if (!ok) break;
+        while (ok && pvs < steps) ok = issue_pv();
+        if (!ok) break;
+        if (last_used < 0) {           // this tile had nothing in the item: release its Q share
+          if (elect_one()) mbar_arrive(&bars->q_empty[qs]);
+          __syncwarp();
+        }
+        if (steps > item_first) ++titems;
+      }
+      if (!ok && lane == 0) fail(abort, 3);
+      // Drain: no MMA may be in flight when TMEM is released.
+      if (elect_one()) mma_commit(&bars->drain);
+      __syncwarp();
+      if (lane == 0) {
         const uint64_t t0 = global_timer_ns();
         while (!mbar_try_wait(&bars->drain, 0) && global_timer_ns() - t0 < kWaitLimitNs) {
         }
       }
+      __syncwarp();
     } else {
       // ------------------------------------------------------------------ softmax + epilogue
-      const int row = threadIdx.x;          // 0..127, TMEM lane
+      const int X = warp >> 2;                 // tile
+      const int row = threadIdx.x & 127;       // TMEM lane
       const int half = row >> 6;
-      const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-      const int32_t f_active = half ? kFlagActive1 : kFlagActive0;
-      const int32_t f_diag = half ? kFlagDiag1 : kFlagDiag0;
+      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+      const uint32_t tcol = tmem + 256 * X;
+      const int shift = kQuadShiftB * X;
+      const int32_t f_tile = kQuadFlagsA << shift;
+      const int32_t f_active = (half ? kFlagActive1 : kFlagActive0) << shift;
+      const int32_t f_diag = (half ? kFlagDiag1 : kFlagDiag0) << shift;
       const int diag_lim = row & 63;
-      uint8_t* prow = smem + kOffP + (row >> 3) * 1024 + (row & 7) * 128;
+      uint8_t* prow = smem + kOffP + (2 * X) * kQBytes + (row >> 3) * 1024 + (row & 7) * 128;
       const int rsw = row & 7;
-      uint32_t it = 0, jj = 0;
+      uint64_t* s_full = bars->s_full[X];
+      uint64_t* p_full = bars->p_full[X];
+      uint64_t* o_done = bars->o_done[X];
+      uint64_t* o_free = &bars->o_free[X];
+      uint32_t it = 0;
       bool ok = true;
-      for (int round = 0; ok; ++round) {
-        const int rank = snake_rank(round, cta, G);
-        if (rank >= L.nitems || *abort) break;
-        const int item = items[rank];
-        const int t = item % L.npairs, bh = item / L.npairs, b = bh / a.H, h = bh % a.H;
-        const int r = L.group_of(b, h) * L.npairs + t;
-        const int e0 = rowptr[r], n = rowptr[r + 1] - e0;
+      for (uint32_t k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!warp_mbar_wait(&bars->item_full[slot], (k >> 1) & 1, abort)) { ok = false; break; }
+        const int item = item_slot[slot];
+        mbar_arrive(&bars->item_empty[slot]);
+        if (item < 0) break;
+        const Item w = decode(a, rowptr, item);
         float m = -INFINITY, l = 0.f;
-        int32_t e_next = n > 0 ? entries[e0] : 0;
-        for (int i = 0; i < n; ++i, ++it) {
+        int nsteps = 0;
+        int32_t e_next = w.n > 0 ? entries[w.e0] : 0;
+        for (int i = 0; i < w.n; ++i) {
           const int32_t e = e_next;
-          if (i + 1 < n) e_next = entries[e0 + i + 1];   // prefetch: off the critical path
-          const uint32_t sb = it & 1;
-          if (!warp_mbar_wait(&bars->s_full[sb], (it >> 1) & 1, abort)) { ok = false; break; }
+          if (i + 1 < w.n) e_next = entries[w.e0 + i + 1];
+          if (!(e & f_tile)) continue;                 // warp-uniform: the chunk is the other tile's
+          ++nsteps;
+          const uint32_t sb = it % 3;
+          if (!warp_mbar_wait(&s_full[sb], (it / 3) & 1, abort)) { ok = false; break; }
           tc_fence_after();
           uint32_t sr[64];
-          XSAKE_TMEM_LD32(tmem + lane_base + 64 * sb, sr);
-          XSAKE_TMEM_LD32(tmem + lane_base + 64 * sb + 32, (sr + 32));
+          XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
+          XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
           XSAKE_TMEM_WAIT_LD32(sr);
           XSAKE_TMEM_WAIT_LD32((sr + 32));
-          tc_fence_before();
-          mbar_arrive(&bars->s_free[sb]);
-          bool waited = false;
           uint32_t pk[32];
           if (e & f_active) {
             float* x = reinterpret_cast<float*>(sr);   // raw scores
@@ -287,25 +389,25 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 #pragma unroll
             for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
             t2[7] = t1[21];
-            const float mraw = fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
+            const float mraw =
+                fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
             const float mx = mraw * p.scale_log2;       // log2 units (scale > 0)
             const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
             if (m == -INFINITY) m = mx;
             // TMEM loads/stores are warp-collective: the whole warp rescales when any row must.
             if (__any_sync(0xffffffffu, need)) {
               // O holds PV of earlier chunks: wait for the last one, then rescale in TMEM.
-              if (!warp_mbar_wait(&bars->o_done, (it - 1) & 1, abort)) { ok = false; break; }
-              waited = true;
+              if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
               tc_fence_after();
               const float alpha = need ? ex2(m - mx) : 1.0f;
               uint32_t orow[32];
 #pragma unroll
               for (int hcol = 0; hcol < 2; ++hcol) {
-                XSAKE_TMEM_LD32(tmem + lane_base + 128 + 32 * hcol, orow);
+                XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
                 XSAKE_TMEM_WAIT_LD32(orow);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
-                XSAKE_TMEM_ST32(tmem + lane_base + 128 + 32 * hcol, orow);
+                XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
               }
               tmem_wait_st();
               if (need) {
@@ -339,68 +441,70 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 #pragma unroll
             for (int j = 0; j < 32; ++j) pk[j] = 0u;
           }
-          // PV of the previous chunk reads the P buffer: wait for it before overwriting.
-          if (it > 0 && !waited && !warp_mbar_wait(&bars->o_done, (it - 1) & 1, abort)) { ok = false; break; }
+          // P buffer it&1 was read by PV(it-2): wait for it before overwriting.
+          const uint32_t pb = it & 1;
+          if (it >= 2 && !warp_mbar_wait(&o_done[pb], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
+          uint8_t* pdst = prow + pb * kQBytes;
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc)
-            *reinterpret_cast<uint4*>(prow + ((cc ^ rsw) << 4)) =
+            *reinterpret_cast<uint4*>(pdst + ((cc ^ rsw) << 4)) =
                 make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
           fence_proxy_async_smem();
           tc_fence_before();
-          mbar_arrive(&bars->p_full);
+          mbar_arrive(&p_full[pb]);
+          ++it;
         }
         if (!ok) break;
         // ---------------------------------------------------------------- epilogue
-        const int tok = 128 * t + row;
+        const int tok = 256 * w.u + 128 * X + row;
         const bool valid = tok < a.S;
         const bool empty = valid && !(l > 0.f);
-        uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + b * a.os[0] +
-                                                 h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
-        if (n > 0) {
-          if (!warp_mbar_wait(&bars->o_done, (it - 1) & 1, abort)) { ok = false; break; }
+        uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + w.b * a.os[0] +
+                                                 w.h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
+        if (nsteps > 0) {
+          if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
           tc_fence_after();
           const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll
           for (int hcol = 0; hcol < 2; ++hcol) {
             uint32_t orow[32];
-            XSAKE_TMEM_LD32(tmem + lane_base + 128 + 32 * hcol, orow);
+            XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
             XSAKE_TMEM_WAIT_LD32(orow);
             if (valid && !empty) {
 #pragma unroll
               for (int cc = 0; cc < 4; ++cc) {
-                uint32_t w[4];
+                uint32_t wv[4];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                   __nv_bfloat162 pb = __floats2bfloat162_rn(__uint_as_float(orow[8 * cc + 2 * q]) * inv,
                                                             __uint_as_float(orow[8 * cc + 2 * q + 1]) * inv);
-                  w[q] = *reinterpret_cast<uint32_t*>(&pb);
+                  wv[q] = *reinterpret_cast<uint32_t*>(&pb);
                 }
-                orow_g[4 * hcol + cc] = make_uint4(w[0], w[1], w[2], w[3]);
+                orow_g[4 * hcol + cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
               }
             }
           }
           tc_fence_before();
-          mbar_arrive(&bars->o_free);
-          ++jj;
+          mbar_arrive(o_free);
         }
         if (__any_sync(0xffffffffu, empty)) {
           // Rows with no live score: the reference's finfo.min fill makes them attend uniformly.
           float2 mine;
-          warp_mean_v(a, b, h, mine);
+          warp_mean_v(a, w.b, w.h, mine);
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc) {
-            uint32_t w[4];
+            uint32_t wv[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int src = 4 * cc + q;   // column pair index 0..31
               __nv_bfloat162 pb = __floats2bfloat162_rn(__shfl_sync(0xffffffffu, mine.x, src),
                                                         __shfl_sync(0xffffffffu, mine.y, src));
-              w[q] = *reinterpret_cast<uint32_t*>(&pb);
+              wv[q] = *reinterpret_cast<uint32_t*>(&pb);
             }
-            if (empty) orow_g[cc] = make_uint4(w[0], w[1], w[2], w[3]);
+            if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
           }
         }
-        if (valid) a.lse[(int64_t)bh * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
+        if (valid) a.lse[(int64_t)(w.b * a.H + w.h) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
       }
       if (!ok) fail(abort, 4);
     }
@@ -458,6 +562,10 @@ int make_map(CUtensorMap* map, const void* base, const int64_t st[3], int B, int
   return XSAKE_OK;
 }
 
+constexpr int kMaxDev = 64;
+std::once_flag g_attr_once[kMaxDev];
+cudaError_t g_attr_err[kMaxDev];
+
 }  // namespace
 
 bool tc_attn_fwd_supported(const AttnArgs& a, int dtype) {
@@ -469,29 +577,35 @@ bool tc_attn_fwd_supported(const AttnArgs& a, int dtype) {
   return aligned(a.q, a.qs) && aligned(a.k, a.ks) && aligned(a.v, a.vs) && aligned(a.o, a.os);
 }
 
-size_t tc_attn_fwd_workspace(const AttnArgs&) { return 0; }
+// The work-item counter of the persistent scheduler.
+size_t tc_attn_fwd_workspace(const AttnArgs&) { return 256; }
 
-int tc_attn_fwd(const AttnArgs& a, void*, size_t, cudaStream_t s) {
+int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   DeviceInfo di;
   int st = device_info(&di);
   if (st) return st;
   XSAKE_REQUIRE(di.major == 10, XSAKE_EUNSUPPORTED, "tensor-core path needs sm_100 (got sm_%d%d)", di.major,
                 di.minor);
+  XSAKE_REQUIRE(ws != nullptr && ws_bytes >= 256 && ((uintptr_t)ws & 15) == 0, XSAKE_EINVAL,
+                "the tensor-core forward needs a 256-byte, 16-byte aligned workspace (got %zu bytes)", ws_bytes);
   CUtensorMap mq, mk, mv;
   if ((st = make_map(&mq, a.q, a.qs, a.B, a.H, a.S, 128))) return st;
   if ((st = make_map(&mk, a.k, a.ks, a.B, a.H, a.S, 64))) return st;
   if ((st = make_map(&mv, a.v, a.vs, a.B, a.H, a.S, 64))) return st;
-  static std::once_flag attr_once;
-  cudaError_t aerr = cudaSuccess;
-  std::call_once(attr_once, [&] {
-    aerr = cudaFuncSetAttribute(tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  int dev = 0;
+  XSAKE_CUDA_TRY(cudaGetDevice(&dev));
+  XSAKE_REQUIRE(dev < kMaxDev, XSAKE_EUNSUPPORTED, "device ordinal %d", dev);
+  std::call_once(g_attr_once[dev], [dev] {
+    g_attr_err[dev] = cudaFuncSetAttribute(tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   });
-  XSAKE_REQUIRE(aerr == cudaSuccess, XSAKE_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(aerr));
+  XSAKE_REQUIRE(g_attr_err[dev] == cudaSuccess, XSAKE_ECUDA, "cudaFuncSetAttribute: %s",
+                cudaGetErrorString(g_attr_err[dev]));
   TcParams p;
   p.a = a;
   p.scale_log2 = a.scale * kLog2e;
-  const int nitems = a.L.nitems;
-  const int grid = std::max(1, std::min(nitems, 2 * di.sm_count));
+  p.counter = reinterpret_cast<int*>(ws);
+  XSAKE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(int), s));
+  const int grid = std::max(1, std::min(a.L.nqitems, di.sm_count));
   tc_fwd_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
   return check_launch("tc_fwd_kernel");
 }
