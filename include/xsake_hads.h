@@ -148,7 +148,7 @@ XSAKE_API int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t head
  * device synchronisation).  It has no counterpart in the reference: the reference never
  * manages device memory itself.  Scratch is a library-owned static device array of 65,536
  * fp64 partial sums (512 KiB on every GPU that loads the library): calls needing more
- * (batch * heads * ctas_per_slice, ctas_per_slice = seq_q / largest divisor of seq_q <= 64)
+ * (batch * heads * ctas_per_slice, ctas_per_slice = seq_q / largest divisor of seq_q <= 16)
  * return XSAKE_EUNSUPPORTED.  The first call on a device resolves the array's address; make it
  * before any stream capture.  All calls share the array, so calls overlapping on the GPU race. */
 XSAKE_API int xsake_entropy_rows_noalloc(const float* p_dev, int64_t batch, int64_t heads,

@@ -69,7 +69,8 @@ def test_noalloc_rejects_sizes_beyond_its_static_scratch():
     lib = _lib.load()
     out = torch.zeros(1, dtype=torch.float64, device="cuda")
     p = torch.zeros(16, dtype=torch.float32, device="cuda")
-    # 2048 * 64 slices of 64 query rows -> 131,072 partial sums > 65,536: refused, nothing launched
+    # 2048 * 64 slices of 64 query rows, 16 rows per partial -> 524,288 partial sums > 65,536:
+    # refused, nothing launched
     st = lib.xsake_entropy_rows_noalloc(p.data_ptr(), 2048, 64, 64, 4, out.data_ptr(),
                                         torch.cuda.current_stream().cuda_stream)
     assert st == _lib.XSAKE_EUNSUPPORTED

@@ -28,44 +28,52 @@ struct EntropyGeom {
   int64_t ctas_per_bh;
 };
 
-// Rows of one CTA: [cta * rows_per_cta, +rows_per_cta) of the flattened [B*H*Sq] rows.
+// Work is cut into chunks of rows_per_cta (<= 16) consecutive rows of one (b, h) slice; chunk c
+// writes partial[c].  A persistent grid gives each CTA a contiguous, balanced range of chunks;
+// each warp reduces two rows of a chunk with all their loads issued up front (eight 16-byte
+// words per row per lane when Sk = 1024), and the chunk's rows are summed in a fixed order, so
+// the partials do not depend on the grid.
 __global__ void __launch_bounds__(256) entropy_rows_kernel(const float* __restrict__ p, EntropyGeom g,
-                                                           double* __restrict__ partial) {
-  __shared__ double swarp[kEntWarps];
+                                                           int64_t nchunks, double* __restrict__ partial) {
+  __shared__ double srow[2][16];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t row0 = (int64_t)blockIdx.x * g.rows_per_cta;
-  double acc = 0.0;
-  const bool vec = (g.Sk % 4) == 0;
-  for (int64_t r = warp; r < g.rows_per_cta; r += kEntWarps) {
-    const float* pr = p + (row0 + r) * g.Sk;
-    float s = 0.f;
-    if (vec) {
-      const float4* p4 = reinterpret_cast<const float4*>(pr);
-      const int64_t nv = g.Sk / 4;
-      int64_t v = lane;
-      for (; v + 96 < nv; v += 128) {
-        const float4 a = p4[v], b = p4[v + 32], c = p4[v + 64], d = p4[v + 96];
-        s += plogp(a.x) + plogp(a.y) + plogp(a.z) + plogp(a.w);
-        s += plogp(b.x) + plogp(b.y) + plogp(b.z) + plogp(b.w);
-        s += plogp(c.x) + plogp(c.y) + plogp(c.z) + plogp(c.w);
-        s += plogp(d.x) + plogp(d.y) + plogp(d.z) + plogp(d.w);
+  const int64_t c0 = nchunks * blockIdx.x / gridDim.x, c1 = nchunks * (blockIdx.x + 1) / gridDim.x;
+  int it = 0;
+  for (int64_t c = c0; c < c1; ++c, ++it) {
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const int r = 2 * warp + rr;
+      double ent = 0.0;
+      if (r < g.rows_per_cta) {
+        const float* pr = p + (c * g.rows_per_cta + r) * g.Sk;
+        float s = 0.f;
+        if (g.Sk == 1024) {
+          const float4* p4 = reinterpret_cast<const float4*>(pr);
+          float4 t[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) t[u] = p4[lane + 32 * u];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) s += plogp(t[u].x) + plogp(t[u].y) + plogp(t[u].z) + plogp(t[u].w);
+        } else if ((g.Sk % 4) == 0) {
+          const float4* p4 = reinterpret_cast<const float4*>(pr);
+          for (int64_t v = lane; v < g.Sk / 4; v += 32) {
+            const float4 a = p4[v];
+            s += plogp(a.x) + plogp(a.y) + plogp(a.z) + plogp(a.w);
+          }
+        } else {
+          for (int64_t k = lane; k < g.Sk; k += 32) s += plogp(pr[k]);
+        }
+        s = warp_sum(s);
+        ent = -(double)s * (double)kLn2;
       }
-      for (; v < nv; v += 32) {
-        const float4 a = p4[v];
-        s += plogp(a.x) + plogp(a.y) + plogp(a.z) + plogp(a.w);
-      }
-    } else {
-      for (int64_t c = lane; c < g.Sk; c += 32) s += plogp(pr[c]);
+      if (lane == 0) srow[it & 1][r] = ent;
     }
-    s = warp_sum(s);
-    acc += -(double)s * (double)kLn2;
-  }
-  if (lane == 0) swarp[warp] = acc;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int w = 0; w < kEntWarps; ++w) t += swarp[w];
-    partial[blockIdx.x] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double t = 0.0;
+      for (int r = 0; r < g.rows_per_cta; ++r) t += srow[it & 1][r];
+      partial[c] = t;
+    }
   }
 }
 
@@ -78,11 +86,18 @@ __global__ void entropy_heads_kernel(const double* __restrict__ partial, Entropy
   head_sums[h] = t;
 }
 
+unsigned entropy_grid(int64_t nchunks) {
+  DeviceInfo di;
+  const int sms = device_info(&di) == XSAKE_OK ? di.sm_count : 148;
+  clear_error();
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(nchunks, (int64_t)sms * 8));
+}
+
 EntropyGeom geom(int64_t B, int64_t H, int64_t Sq, int64_t Sk) {
   EntropyGeom g{B, H, Sq, Sk, 1, 1};
-  // Aim for ~64 rows per CTA, keeping rows_per_cta a divisor of Sq.
+  // Chunks of up to 16 rows (a divisor of Sq), two rows per warp.
   int64_t rpc = 1;
-  for (int64_t c = std::min<int64_t>(64, Sq); c >= 1; --c)
+  for (int64_t c = std::min<int64_t>(16, Sq); c >= 1; --c)
     if (Sq % c == 0) { rpc = c; break; }
   g.rows_per_cta = rpc;
   g.ctas_per_bh = Sq / rpc;
@@ -116,7 +131,7 @@ extern "C" int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t hea
                 "workspace too small: %zu < %zu bytes", workspace_bytes, (size_t)nctas * sizeof(double));
   cudaStream_t s = as_stream(stream);
   double* partial = reinterpret_cast<double*>(workspace_dev);
-  entropy_rows_kernel<<<(unsigned)nctas, 256, 0, s>>>(p_dev, g, partial);
+  entropy_rows_kernel<<<entropy_grid(nctas), 256, 0, s>>>(p_dev, g, nctas, partial);
   int st = check_launch("entropy_rows_kernel");
   if (st) return st;
   entropy_heads_kernel<<<(unsigned)((heads + 127) / 128), 128, 0, s>>>(partial, g, head_sums_dev);
@@ -136,7 +151,7 @@ extern "C" int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t hea
 // Limits and behaviour:
 //   * at most kNoAllocMaxPartials = 65,536 partial sums (512 KiB, held by every GPU that loads
 //     the library until the process exits): batch * heads * ctas_per_slice must not exceed it,
-//     where ctas_per_slice = seq_q / (largest divisor of seq_q that is <= 64); larger calls are
+//     where ctas_per_slice = seq_q / (largest divisor of seq_q that is <= 16); larger calls are
 //     rejected with XSAKE_EUNSUPPORTED before anything is launched;
 //   * the first call on each device looks up the array's device address with
 //     cudaGetSymbolAddress (with that device current); make that first call before any stream
@@ -188,7 +203,7 @@ extern "C" int xsake_entropy_rows_noalloc(const float* p_dev, int64_t batch, int
   int st = partials_address(&partial);
   if (st) return st;
   cudaStream_t s = as_stream(stream);
-  entropy_rows_kernel<<<(unsigned)nctas, 256, 0, s>>>(p_dev, g, partial);
+  entropy_rows_kernel<<<entropy_grid(nctas), 256, 0, s>>>(p_dev, g, nctas, partial);
   if ((st = check_launch("entropy_rows_kernel"))) return st;
   entropy_heads_kernel<<<(unsigned)((heads + 127) / 128), 128, 0, s>>>(partial, g, head_sums_dev);
   return check_launch("entropy_heads_kernel");

@@ -19,6 +19,9 @@ namespace {
 template <typename T> struct Vec;
 template <> struct Vec<float> {
   static constexpr int N = 4;
+  __device__ static void from_raw(const uint4& r, float* x) {
+    x[0] = __uint_as_float(r.x); x[1] = __uint_as_float(r.y); x[2] = __uint_as_float(r.z); x[3] = __uint_as_float(r.w);
+  }
   __device__ static void load(const void* p, float* x) {
     const float4 v = *reinterpret_cast<const float4*>(p);
     x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
@@ -29,6 +32,15 @@ template <> struct Vec<float> {
 };
 template <> struct Vec<__nv_bfloat16> {
   static constexpr int N = 8;
+  __device__ static void from_raw(const uint4& v, float* x) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+      x[2 * i] = __bfloat162float(b.x);
+      x[2 * i + 1] = __bfloat162float(b.y);
+    }
+  }
   __device__ static void load(const void* p, float* x) {
     const uint4 v = *reinterpret_cast<const uint4*>(p);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -180,31 +192,49 @@ __global__ void __launch_bounds__(256) layernorm_fwd_reg(const T* __restrict__ x
   constexpr int N = Vec<T>::N;
   const int lane = threadIdx.x & 31;
   const int64_t nvec = d / N;
+  // gamma/beta: staged once per CTA in shared memory with coalesced 16-byte loads.
+  extern __shared__ float4 sgb[];                 // [2][d/4]
+  for (int64_t i = threadIdx.x; i < d / 4; i += blockDim.x) {
+    sgb[i] = reinterpret_cast<const float4*>(gamma)[i];
+    sgb[d / 4 + i] = reinterpret_cast<const float4*>(beta)[i];
+  }
+  __syncthreads();
+  const float* sg = reinterpret_cast<const float*>(sgb);
+  const float* sbt = sg + d;
   float g[VPL][N], bt[VPL][N];
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
     const int64_t vi = lane + 32 * k;
 #pragma unroll
     for (int i = 0; i < N; ++i) {
-      g[k][i] = vi < nvec ? gamma[vi * N + i] : 0.f;
-      bt[k][i] = vi < nvec ? beta[vi * N + i] : 0.f;
+      g[k][i] = vi < nvec ? sg[vi * N + i] : 0.f;
+      bt[k][i] = vi < nvec ? sbt[vi * N + i] : 0.f;
     }
   }
   const float inv_d = 1.f / (float)d;
-  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
-       row += (int64_t)gridDim.x * kWarpsPerBlock) {
-    const T* xr = x + row * d;
+  const int64_t stride = (int64_t)gridDim.x * kWarpsPerBlock;
+  int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  // Rows are software-pipelined: the next row's 16-byte words are in flight while this row is
+  // normalised, so each warp keeps two rows of loads outstanding.
+  uint4 nxt[VPL];
+  auto fetch = [&](int64_t r) {
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      nxt[k] = (r < rows && vi < nvec) ? *reinterpret_cast<const uint4*>(x + r * d + vi * N) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  fetch(row);
+  for (; row < rows; row += stride) {
+    uint4 cur[VPL];
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) cur[k] = nxt[k];
+    fetch(row + stride);
     float v[VPL][N];
     float s = 0.f;
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
-      const int64_t vi = lane + 32 * k;
-      if (vi < nvec) {
-        Vec<T>::load(xr + vi * N, v[k]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < N; ++i) v[k][i] = 0.f;
-      }
+      Vec<T>::from_raw(cur[k], v[k]);
 #pragma unroll
       for (int i = 0; i < N; ++i) s += v[k][i];
     }
@@ -327,9 +357,9 @@ __global__ void ln_bwd_reduce(const float* __restrict__ partial, int nblocks, in
   if (c < d) dgamma[c] = acc; else dbeta[c - d] = acc;
 }
 
-int grid_for_rows(int64_t rows, int sm_count) {
+int grid_for_rows(int64_t rows, int sm_count, int ctas_per_sm = 32) {
   const int64_t blocks = (rows + kWarpsPerBlock - 1) / kWarpsPerBlock;
-  return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sm_count * 32));
+  return (int)std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)sm_count * ctas_per_sm));
 }
 
 template <typename T>
@@ -371,14 +401,16 @@ int layernorm_fwd_t(int64_t rows, int64_t d, const void* x, const float* g, cons
   constexpr int N = Vec<T>::N;
   const T* xp = reinterpret_cast<const T*>(x);
   T* yp = reinterpret_cast<T*>(y);
-  const int grid = grid_for_rows(rows, sms);
-  const bool vec_ok = d % N == 0 && (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+  // Several rows per warp: gamma/beta reach registers once per warp (from shared memory).
+  const int grid = grid_for_rows(rows, sms, 8);
+  const bool vec_ok = d % N == 0 && d % 4 == 0 && (((uintptr_t)x | (uintptr_t)y | (uintptr_t)g | (uintptr_t)b) & 15) == 0;
   const int64_t per_lane = (d / N + 31) / 32;
-  if (vec_ok && per_lane <= 1) layernorm_fwd_reg<T, 1><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else if (vec_ok && per_lane <= 2) layernorm_fwd_reg<T, 2><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else if (vec_ok && per_lane <= 3) layernorm_fwd_reg<T, 3><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else if (vec_ok && per_lane <= 4) layernorm_fwd_reg<T, 4><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else if (vec_ok && per_lane <= 8) layernorm_fwd_reg<T, 8><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  const size_t smem = 2 * (size_t)d * sizeof(float);
+  if (vec_ok && per_lane <= 1) layernorm_fwd_reg<T, 1><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else if (vec_ok && per_lane <= 2) layernorm_fwd_reg<T, 2><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else if (vec_ok && per_lane <= 3) layernorm_fwd_reg<T, 3><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else if (vec_ok && per_lane <= 4) layernorm_fwd_reg<T, 4><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  else if (vec_ok && per_lane <= 8) layernorm_fwd_reg<T, 8><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
   else layernorm_fwd_generic<T><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
   return check_launch("layernorm_fwd");
 }
