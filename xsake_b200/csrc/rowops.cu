@@ -192,30 +192,11 @@ __global__ void __launch_bounds__(256) layernorm_fwd_reg(const T* __restrict__ x
   constexpr int N = Vec<T>::N;
   const int lane = threadIdx.x & 31;
   const int64_t nvec = d / N;
-  // gamma/beta: staged once per CTA in shared memory with coalesced 16-byte loads.
-  extern __shared__ float4 sgb[];                 // [2][d/4]
-  for (int64_t i = threadIdx.x; i < d / 4; i += blockDim.x) {
-    sgb[i] = reinterpret_cast<const float4*>(gamma)[i];
-    sgb[d / 4 + i] = reinterpret_cast<const float4*>(beta)[i];
-  }
-  __syncthreads();
-  const float* sg = reinterpret_cast<const float*>(sgb);
-  const float* sbt = sg + d;
-  float g[VPL][N], bt[VPL][N];
-#pragma unroll
-  for (int k = 0; k < VPL; ++k) {
-    const int64_t vi = lane + 32 * k;
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-      g[k][i] = vi < nvec ? sg[vi * N + i] : 0.f;
-      bt[k][i] = vi < nvec ? sbt[vi * N + i] : 0.f;
-    }
-  }
-  const float inv_d = 1.f / (float)d;
   const int64_t stride = (int64_t)gridDim.x * kWarpsPerBlock;
   int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
   // Rows are software-pipelined: the next row's 16-byte words are in flight while this row is
-  // normalised, so each warp keeps two rows of loads outstanding.
+  // normalised, so each warp keeps two rows of loads outstanding.  The first row's loads are
+  // issued before gamma/beta are staged so the two latencies overlap.
   uint4 nxt[VPL];
   auto fetch = [&](int64_t r) {
 #pragma unroll
@@ -225,6 +206,18 @@ __global__ void __launch_bounds__(256) layernorm_fwd_reg(const T* __restrict__ x
     }
   };
   fetch(row);
+  // gamma/beta: staged once per CTA in shared memory with coalesced 16-byte loads and read back
+  // where each output is formed (keeping them in registers would cost 2 * VPL * N registers a
+  // thread and halve the resident warps).
+  extern __shared__ float4 sgb[];                 // [2][d/4]
+  for (int64_t i = threadIdx.x; i < d / 4; i += blockDim.x) {
+    sgb[i] = reinterpret_cast<const float4*>(gamma)[i];
+    sgb[d / 4 + i] = reinterpret_cast<const float4*>(beta)[i];
+  }
+  __syncthreads();
+  const float4* sg4 = sgb;
+  const float4* sb4 = sgb + d / 4;
+  const float inv_d = 1.f / (float)d;
   for (; row < rows; row += stride) {
     uint4 cur[VPL];
 #pragma unroll
@@ -258,7 +251,13 @@ __global__ void __launch_bounds__(256) layernorm_fwd_reg(const T* __restrict__ x
       if (vi < nvec) {
         float o[N];
 #pragma unroll
-        for (int i = 0; i < N; ++i) o[i] = fmaf(g[k][i], (v[k][i] - mean) * rstd, bt[k][i]);
+        for (int j = 0; j < N / 4; ++j) {
+          const float4 g = sg4[vi * (N / 4) + j], b = sb4[vi * (N / 4) + j];
+          o[4 * j + 0] = fmaf(g.x, (v[k][4 * j + 0] - mean) * rstd, b.x);
+          o[4 * j + 1] = fmaf(g.y, (v[k][4 * j + 1] - mean) * rstd, b.y);
+          o[4 * j + 2] = fmaf(g.z, (v[k][4 * j + 2] - mean) * rstd, b.z);
+          o[4 * j + 3] = fmaf(g.w, (v[k][4 * j + 3] - mean) * rstd, b.w);
+        }
         Vec<T>::store(yr + vi * N, o);
       }
     }
@@ -401,17 +400,25 @@ int layernorm_fwd_t(int64_t rows, int64_t d, const void* x, const float* g, cons
   constexpr int N = Vec<T>::N;
   const T* xp = reinterpret_cast<const T*>(x);
   T* yp = reinterpret_cast<T*>(y);
-  // Several rows per warp: gamma/beta reach registers once per warp (from shared memory).
-  const int grid = grid_for_rows(rows, sms, 8);
   const bool vec_ok = d % N == 0 && d % 4 == 0 && (((uintptr_t)x | (uintptr_t)y | (uintptr_t)g | (uintptr_t)b) & 15) == 0;
   const int64_t per_lane = (d / N + 31) / 32;
   const size_t smem = 2 * (size_t)d * sizeof(float);
-  if (vec_ok && per_lane <= 1) layernorm_fwd_reg<T, 1><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else if (vec_ok && per_lane <= 2) layernorm_fwd_reg<T, 2><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else if (vec_ok && per_lane <= 3) layernorm_fwd_reg<T, 3><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else if (vec_ok && per_lane <= 4) layernorm_fwd_reg<T, 4><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else if (vec_ok && per_lane <= 8) layernorm_fwd_reg<T, 8><<<grid, 256, smem, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
-  else layernorm_fwd_generic<T><<<grid, 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  // One wave: as many CTAs as fit on the GPU at once (each stages gamma/beta once and then
+  // normalises rows/grid rows per warp).
+  auto launch = [&](auto kern, size_t sm) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, sm) != cudaSuccess || per_sm < 1) {
+      (void)cudaGetLastError();
+      per_sm = 2;
+    }
+    kern<<<grid_for_rows(rows, sms, per_sm), 256, sm, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
+  };
+  if (vec_ok && per_lane <= 1) launch(layernorm_fwd_reg<T, 1>, smem);
+  else if (vec_ok && per_lane <= 2) launch(layernorm_fwd_reg<T, 2>, smem);
+  else if (vec_ok && per_lane <= 3) launch(layernorm_fwd_reg<T, 3>, smem);
+  else if (vec_ok && per_lane <= 4) launch(layernorm_fwd_reg<T, 4>, smem);
+  else if (vec_ok && per_lane <= 8) launch(layernorm_fwd_reg<T, 8>, smem);
+  else layernorm_fwd_generic<T><<<grid_for_rows(rows, sms, 8), 256, 0, s>>>(xp, g, b, eps, yp, mean, rstd, rows, d);
   return check_launch("layernorm_fwd");
 }
 
