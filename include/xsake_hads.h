@@ -102,7 +102,9 @@ XSAKE_API int xsake_attn_fwd(const XsakeAttnDesc* desc, const void* plan_dev, co
                    void* workspace_dev, size_t workspace_bytes, void* stream);
 
 /* Backward of the above (the reference has no VJP; this is autodiff of
- * sparse_attention_reference, :45-91).  lse_dev is the forward's output. */
+ * sparse_attention_reference, :45-91).  lse_dev is the forward's output.  The workspace must
+ * be 256-byte aligned.  bf16 / head_dim 64 / block_size % 64 == 0 runs on the tensor cores
+ * (deterministic: no atomics on the gradients); other configurations on CUDA cores. */
 XSAKE_API int xsake_attn_bwd_workspace_size(const XsakeAttnDesc* desc, size_t* bytes);
 XSAKE_API int xsake_attn_bwd(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
                    const void* k_dev, const void* v_dev, const void* o_dev,

@@ -184,6 +184,90 @@ def test_backward_matches_oracle(dtype):
         assert _err(g, ref) <= tol * scale, (_err(g, ref), scale)
 
 
+def _bf16_bwd_case(B, H, S, D, bs, causal, mask, seed, layout="bhsd", scale=None):
+    """bf16 backward (the tensor-core kernels for D=64 and 64-multiple blocks) against the
+    float64 closed form on the same bf16-rounded inputs: max|err| <= 2e-2 * max|ref|."""
+    sa = _sa()
+    q, k, v, do = (_bf16_round(_rand((B, H, S, D), seed + i)) for i in range(4))
+    tq, tk, tv, tdo = (torch.from_numpy(x).to(torch.bfloat16).cuda() for x in (q, k, v, do))
+    if layout == "bshd":
+        tq, tk, tv, tdo = (t.transpose(1, 2).contiguous().transpose(1, 2) for t in (tq, tk, tv, tdo))
+    o, lse = sa.attention_forward(tq, tk, tv, mask, bs, scale, causal)
+    if layout == "bshd":
+        o = o.transpose(1, 2).contiguous().transpose(1, 2)
+    dq, dk, dv = sa.attention_backward(tq, tk, tv, o, lse, tdo, mask, bs, scale, causal)
+    rq, rk, rv = oa.sparse_attention_backward(q, k, v, do, mask, bs, scale=scale, causal=causal)
+    for name, got, ref in (("dq", dq, rq), ("dk", dk, rk), ("dv", dv, rv)):
+        g = got.float().cpu().numpy()
+        assert np.isfinite(g).all(), name
+        assert _err(g, ref) <= BF16_TOL * np.abs(ref).max(), (name, _err(g, ref), np.abs(ref).max())
+    return dq, dk, dv
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("global_blocks", [0, 1])
+def test_bf16_backward_tensor_core_hads(causal, global_blocks):
+    prof = oh.dummy_hads_profile(4, 512, 64, causal=causal, global_blocks=global_blocks)
+    _bf16_bwd_case(2, 4, 512, 64, 64, causal, prof.block_masks, seed=70)
+
+
+def test_bf16_backward_block128_and_shared_mask():
+    prof = oh.dummy_hads_profile(3, 1024, 128, causal=True)
+    _bf16_bwd_case(1, 3, 1024, 64, 128, True, prof.block_masks, seed=80)
+    shared = oh.build_head_mask(0.5, 8, 1, 3, causal=True)
+    _bf16_bwd_case(2, 2, 512, 64, 64, True, shared, seed=81)
+
+
+def test_bf16_backward_odd_chunk_count_and_empty_rows():
+    # S = 320: the last 128-key and 128-query tiles are half outside the sequence; a fully
+    # masked q-block sends dO/S to every key's dV and nothing to dQ/dK.
+    m = oh.dummy_hads_profile(2, 320, 64, causal=True).block_masks.copy()
+    m[1, 2, :] = False
+    m[0, 4, :4] = False
+    _bf16_bwd_case(1, 2, 320, 64, 64, True, m, seed=90)
+
+
+def test_bf16_backward_bshd_layout_and_scale():
+    prof = oh.dummy_hads_profile(4, 256, 64, causal=True)
+    _bf16_bwd_case(2, 4, 256, 64, 64, True, prof.block_masks, seed=100, layout="bshd", scale=0.2)
+
+
+def test_bf16_backward_simt_fallback_shapes():
+    prof = oh.dummy_hads_profile(4, 256, 32, causal=True)
+    _bf16_bwd_case(1, 4, 256, 32, 32, True, prof.block_masks, seed=110)
+
+
+def test_backward_is_deterministic():
+    sa = _sa()
+    prof = oh.dummy_hads_profile(12, 2048, 64, causal=True, global_blocks=1)
+    q, k, v, do = (torch.randn(2, 12, 2048, 64, device="cuda", dtype=torch.bfloat16) for _ in range(4))
+    o, lse = sa.attention_forward(q, k, v, prof.block_masks, 64, None, True)
+    g1 = sa.attention_backward(q, k, v, o, lse, do, prof.block_masks, 64, None, True)
+    g2 = sa.attention_backward(q, k, v, o, lse, do, prof.block_masks, 64, None, True)
+    for a, b in zip(g1, g2):
+        assert torch.equal(a, b)
+
+
+def test_backward_config3_full_size_slices():
+    """Backward at config 3 size (bf16 B=4 H=12 S=4096 D=64); the float64 closed form checks a
+    sample of (b, h) slices."""
+    sa = _sa()
+    prof = oh.dummy_hads_profile(12, 4096, 64, causal=True, global_blocks=1)
+    q, k, v = oi.qkv(4, 12, 4096, 64, seed=oi.SEED_BASE + 3)
+    do = _rand((4, 12, 4096, 64), 123)
+    q, k, v, do = (_bf16_round(x) for x in (q, k, v, do))
+    tq, tk, tv, tdo = (torch.from_numpy(x).to(torch.bfloat16).cuda() for x in (q, k, v, do))
+    o, lse = sa.attention_forward(tq, tk, tv, prof.block_masks, 64, None, True)
+    dq, dk, dv = (t.float().cpu().numpy() for t in sa.attention_backward(tq, tk, tv, o, lse, tdo,
+                                                                          prof.block_masks, 64, None, True))
+    for (b, h) in [(0, 0), (3, 11), (2, 7)]:
+        sl = (slice(b, b + 1), slice(h, h + 1))
+        rq, rk, rv = oa.sparse_attention_backward(q[sl], k[sl], v[sl], do[sl], prof.block_masks[h:h + 1], 64,
+                                                  causal=True)
+        for name, got, ref in (("dq", dq[sl], rq), ("dk", dk[sl], rk), ("dv", dv[sl], rv)):
+            assert _err(got, ref) <= BF16_TOL * np.abs(ref).max(), (name, b, h, _err(got, ref))
+
+
 def test_autograd_function_matches_backward():
     sa = _sa()
     prof = oh.dummy_hads_profile(2, 256, 64, causal=True)

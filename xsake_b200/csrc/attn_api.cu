@@ -1,7 +1,8 @@
 // C-ABI entry points of the attention path: argument validation and kernel selection.
 //   bf16, head_dim 64, block_size % 64 == 0, 16-byte aligned rows -> tensor-core forward
 //   everything else (fp32, other head dims or block sizes)       -> CUDA-core kernels
-// The backward runs on the CUDA-core kernels for every configuration.
+// The backward follows the same split: tensor-core kernels for bf16 / head_dim 64 / 64-multiple
+// blocks with 16-byte aligned rows, CUDA-core kernels otherwise.
 // Every kernel checks the plan header against the call (DEV_ERR_PLAN on mismatch).
 #include "attn_common.cuh"
 
@@ -76,7 +77,10 @@ extern "C" int xsake_attn_bwd_workspace_size(const XsakeAttnDesc* desc, size_t* 
   clear_error();
   XSAKE_REQUIRE(desc && bytes, XSAKE_EINVAL, "NULL argument");
   const int64_t bh = (int64_t)desc->batch * desc->heads;
-  *bytes = align_up((size_t)(bh * desc->seq) * 4, 256) + align_up((size_t)(bh * desc->head_dim) * 4, 256);
+  // delta [B*H*S] | ucol [B*H*D] | -lse*log2e [B*H*S] | work-item counters; the CUDA-core
+  // backward uses the first two sections.
+  const size_t rows = align_up((size_t)(bh * desc->seq) * 4, 256);
+  *bytes = 2 * rows + align_up((size_t)(bh * desc->head_dim) * 4, 256) + 256;
   return XSAKE_OK;
 }
 
@@ -103,8 +107,11 @@ extern "C" int xsake_attn_bwd(const XsakeAttnDesc* desc, const void* plan_dev, c
   a.dq = dq_dev;
   a.dk = dk_dev;
   a.dv = dv_dev;
+  XSAKE_REQUIRE(((uintptr_t)workspace_dev & 255) == 0, XSAKE_EINVAL, "workspace must be 256-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  if (tc_attn_bwd_supported(a, desc->dtype)) return tc_attn_bwd(a, workspace_dev, workspace_bytes, s);
   const int64_t bh = (int64_t)a.B * a.H;
   a.delta = reinterpret_cast<float*>(workspace_dev);
   a.ucol = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace_dev) + align_up((size_t)(bh * a.S) * 4, 256));
-  return simt_attn_bwd(a, desc->dtype, as_stream(stream));
+  return simt_attn_bwd(a, desc->dtype, s);
 }

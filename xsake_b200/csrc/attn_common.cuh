@@ -1,6 +1,8 @@
 // Arguments shared by the attention kernels and their host launchers.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 #include "plan.cuh"
 
@@ -41,5 +43,11 @@ int simt_attn_bwd(const AttnArgs& a, int dtype, cudaStream_t s);
 int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
 size_t tc_attn_fwd_workspace(const AttnArgs& a);
 bool tc_attn_fwd_supported(const AttnArgs& a, int dtype);
+int tc_attn_bwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
+bool tc_attn_bwd_supported(const AttnArgs& a, int dtype);
+
+// 4-D bf16 TMA map over [B, H, S, 64] with (b, h, s) element strides; box = rows x 64,
+// SWIZZLE_128B.  Defined in attn_fwd_tc.cu.
+int tc_make_map(CUtensorMap* map, const void* base, const int64_t st[3], int B, int H, int S, int rows);
 
 }  // namespace xsake

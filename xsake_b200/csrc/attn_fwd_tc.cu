@@ -518,7 +518,14 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   }
 }
 
+constexpr int kMaxDev = 64;
+std::once_flag g_attr_once[kMaxDev];
+cudaError_t g_attr_err[kMaxDev];
+
+}  // namespace
+
 // ------------------------------------------------------------------------------ host side
+namespace {
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
@@ -537,9 +544,11 @@ int get_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
   return XSAKE_OK;
 }
 
+}  // namespace
+
 // 4-D bf16 map over [B, H, S, 64] with arbitrary (b, h, s) strides; box = `rows` x 64.
 // Dimensions are ordered by increasing stride, as the tiled TMA layout expects.
-int make_map(CUtensorMap* map, const void* base, const int64_t st[3], int B, int H, int S, int rows) {
+int tc_make_map(CUtensorMap* map, const void* base, const int64_t st[3], int B, int H, int S, int rows) {
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   int s = get_encoder(&enc);
   if (s) return s;
@@ -562,12 +571,6 @@ int make_map(CUtensorMap* map, const void* base, const int64_t st[3], int B, int
   return XSAKE_OK;
 }
 
-constexpr int kMaxDev = 64;
-std::once_flag g_attr_once[kMaxDev];
-cudaError_t g_attr_err[kMaxDev];
-
-}  // namespace
-
 bool tc_attn_fwd_supported(const AttnArgs& a, int dtype) {
   if (dtype != XSAKE_BF16 || a.D != 64 || !a.L.has_csr) return false;
   auto aligned = [](const void* ptr, const int64_t* st) {
@@ -589,9 +592,9 @@ int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   XSAKE_REQUIRE(ws != nullptr && ws_bytes >= 256 && ((uintptr_t)ws & 15) == 0, XSAKE_EINVAL,
                 "the tensor-core forward needs a 256-byte, 16-byte aligned workspace (got %zu bytes)", ws_bytes);
   CUtensorMap mq, mk, mv;
-  if ((st = make_map(&mq, a.q, a.qs, a.B, a.H, a.S, 128))) return st;
-  if ((st = make_map(&mk, a.k, a.ks, a.B, a.H, a.S, 64))) return st;
-  if ((st = make_map(&mv, a.v, a.vs, a.B, a.H, a.S, 64))) return st;
+  if ((st = tc_make_map(&mq, a.q, a.qs, a.B, a.H, a.S, 128))) return st;
+  if ((st = tc_make_map(&mk, a.k, a.ks, a.B, a.H, a.S, 64))) return st;
+  if ((st = tc_make_map(&mv, a.v, a.vs, a.B, a.H, a.S, 64))) return st;
   int dev = 0;
   XSAKE_CUDA_TRY(cudaGetDevice(&dev));
   XSAKE_REQUIRE(dev < kMaxDev, XSAKE_EUNSUPPORTED, "device ordinal %d", dev);
