@@ -10,10 +10,14 @@
 //
 // Work item = 256 query rows of one (b, h): tile A = 64-row chunks (4u, 4u+1), tile B =
 // (4u+2, 4u+3).  The item walks the merged, ascending list of 64-key chunks either tile
-// attends; each chunk's K/V tile is loaded once (TMA, SWIZZLE_128B) into an 8-stage ring and
+// attends; each chunk's K/V tile is loaded once (TMA, SWIZZLE_128B) into a 9-stage ring and
 // used by both tiles when both attend it.  Per tile and chunk: S = Q K^T (tcgen05, M=128 N=64
-// K=64, fp32 in TMEM), softmax by one thread per query row straight out of TMEM, P (bf16) to
-// shared memory, O += P V (tcgen05, fp32 accumulator resident in TMEM).
+// K=64, fp32 in TMEM), softmax by one thread per query row straight out of TMEM, P (bf16)
+// written back into TMEM over the first 32 columns of the scores it came from, O += P V
+// (tcgen05 with A read from TMEM, fp32 accumulator resident in TMEM).  Keeping P out of shared
+// memory matters: an M=128 N=64 K=16 MMA with both operands in shared memory reads 6 KB of it
+// and is bound by shared-memory bandwidth (~50 cycles); with A in TMEM it reads 2 KB and runs at
+// the tensor rate (~35 cycles), and the P stores and their proxy fence disappear.
 // Roles (352 threads, one CTA per SM, persistent):
 //   warps 0-3  softmax + epilogue of tile A (thread i owns row i = TMEM lane i)
 //   warps 4-7  softmax + epilogue of tile B
@@ -23,8 +27,9 @@
 //              is queued before its PV of chunk i-1; a ring stage is released once both
 //              warps are done with it
 // TMEM: 512 columns; per tile (at 256*tile) three S buffers [0,64) [64,128) [128,192) so QK
-// runs two chunks ahead of the softmax, and O at [192,256).  P is double-buffered in shared
-// memory, so the softmax of chunk s only needs the PV of chunk s-2 to have finished.
+// runs two chunks ahead of the softmax, and O at [192,256).  P of chunk s lives in S buffer s%3;
+// the MMA warp issues QK of chunk s+3 (which overwrites it) only after PV of chunk s, and one
+// thread's MMAs execute in issue order.
 // The running max is only moved when it grows by more than 2^8 (rescaling O in TMEM is then
 // rare); exp2 runs on MUFU for 5/8 of the elements and on a cubic polynomial for the rest.
 #include "attn_common.cuh"
@@ -41,14 +46,13 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kStages = 6;
+constexpr int kStages = 9;
 constexpr int kThreads = 352;
 constexpr int kQBytes = 128 * 64 * 2;
 constexpr int kKBytes = 64 * 64 * 2;
 constexpr int kStageBytes = 2 * kKBytes;
 constexpr int kOffQ = 0;                              // [2 slots][2 tiles]
-constexpr int kOffP = kOffQ + 4 * kQBytes;            // [2 tiles][2 buffers]
-constexpr int kOffKV = kOffP + 4 * kQBytes;           // [kStages] K then V
+constexpr int kOffKV = kOffQ + 4 * kQBytes;           // [kStages] K then V
 constexpr int kOffBar = kOffKV + kStages * kStageBytes;
 
 struct Bars {
@@ -56,7 +60,8 @@ struct Bars {
   uint64_t q_full[2], q_empty[2];
   uint64_t kv_full[kStages], kv_empty[kStages];
   uint64_t s_full[2][3];                 // [tile][S buffer]
-  uint64_t p_full[2][2], o_done[2][2];   // [tile][P buffer]
+  uint64_t p_full[2][3];                 // [tile][S buffer holding P]
+  uint64_t o_done[2][2];                 // [tile][PV parity]
   uint64_t o_free[2];
   uint64_t drain;
 };
@@ -133,10 +138,8 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
       mbar_init(&bars->q_full[s], 1);
       mbar_init(&bars->q_empty[s], 2);        // one release per tile's MMA warp
       mbar_init(&bars->o_free[s], 128);
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(&bars->p_full[s][b], 128);
-        mbar_init(&bars->o_done[s][b], 1);
-      }
+      for (int b = 0; b < 2; ++b) mbar_init(&bars->o_done[s][b], 1);
+      for (int b = 0; b < 3; ++b) mbar_init(&bars->p_full[s][b], 128);
       for (int b = 0; b < 3; ++b) mbar_init(&bars->s_full[s][b], 1);
     }
     for (int s = 0; s < kStages; ++s) {
@@ -233,24 +236,22 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
       const int X = warp - 9;
       const int32_t f_tile = kQuadFlagsA << (kQuadShiftB * X);
       const uint32_t tcol = tmem + 256 * X;
-      const uint64_t pdesc0 = sw128_desc(smem_u32(smem + kOffP + (2 * X) * kQBytes), 16, 1024);
       const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV), 16, 1024);
       uint32_t it = 0, qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
       int pstage[3] = {0, 0, 0};
       bool ok = true;
       auto issue_pv = [&]() -> bool {
-        const uint32_t s = pvs, pb = s & 1;
-        if (!warp_mbar_wait(&bars->p_full[X][pb], (s >> 1) & 1, abort)) return false;
+        const uint32_t s = pvs, pb = s & 1, sbuf = s % 3;
+        if (!warp_mbar_wait(&bars->p_full[X][sbuf], (s / 3) & 1, abort)) return false;
         const bool first = (s == item_first);
         if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
         tc_fence_after();
-        const int st = pstage[s % 3];
+        const int st = pstage[sbuf];
         if (elect_one()) {
-          const uint64_t pdesc = pdesc0 + (uint64_t)((pb * kQBytes) >> 4);
           const uint64_t vdesc = kdesc0 + (uint64_t)((st * kStageBytes + kKBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_bf16_ss(tcol + 192, pdesc + 2 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
+          for (int kk = 0; kk < 4; ++kk)   // O += P V, P = 16 keys per 8 TMEM columns
+            mma_bf16_ts(tcol + 192, tcol + 64 * sbuf + 8 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
                         (first && kk == 0) ? 0u : 1u);
           mma_commit(&bars->o_done[X][pb]);
           mma_commit(&bars->kv_empty[st]);
@@ -341,8 +342,6 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
       const int32_t f_active = (half ? kFlagActive1 : kFlagActive0) << shift;
       const int32_t f_diag = (half ? kFlagDiag1 : kFlagDiag0) << shift;
       const int diag_lim = row & 63;
-      uint8_t* prow = smem + kOffP + (2 * X) * kQBytes + (row >> 3) * 1024 + (row & 7) * 128;
-      const int rsw = row & 7;
       uint64_t* s_full = bars->s_full[X];
       uint64_t* p_full = bars->p_full[X];
       uint64_t* o_done = bars->o_done[X];
@@ -441,17 +440,11 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 #pragma unroll
             for (int j = 0; j < 32; ++j) pk[j] = 0u;
           }
-          // P buffer it&1 was read by PV(it-2): wait for it before overwriting.
-          const uint32_t pb = it & 1;
-          if (it >= 2 && !warp_mbar_wait(&o_done[pb], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
-          uint8_t* pdst = prow + pb * kQBytes;
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc)
-            *reinterpret_cast<uint4*>(pdst + ((cc ^ rsw) << 4)) =
-                make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
-          fence_proxy_async_smem();
+          // P over the first 32 columns of the S buffer this thread has just read (its own row).
+          XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
+          tmem_wait_st();
           tc_fence_before();
-          mbar_arrive(&p_full[pb]);
+          mbar_arrive(&p_full[sb]);
           ++it;
         }
         if (!ok) break;
@@ -462,6 +455,12 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + w.b * a.os[0] +
                                                  w.h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
         if (nsteps > 0) {
+          // PV(s) completes phase s/2 of o_done[s % 2].  A parity wait for PV(it-1) is only
+          // unambiguous if that barrier's previous phase (PV(it-3)) has completed; the last S
+          // buffer seen (QK(it-1)) only implies PV(it-4).  So wait for PV(it-2) first (its
+          // previous phase, PV(it-4), is known complete), which implies PV(it-3), then PV(it-1).
+          // (Inside the loop the rescale at step it is safe: QK(it) implies PV(it-3).)
+          if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
           if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
           tc_fence_after();
           const float inv = l > 0.f ? 1.f / l : 0.f;
