@@ -31,7 +31,7 @@
 // the MMA warp issues QK of chunk s+3 (which overwrites it) only after PV of chunk s, and one
 // thread's MMAs execute in issue order.
 // The running max is only moved when it grows by more than 2^8 (rescaling O in TMEM is then
-// rare); exp2 runs on MUFU for 5/8 of the elements and on a cubic polynomial for the rest.
+// rare); exp2 runs on MUFU for 3/4 of the elements and on a cubic polynomial for the rest.
 #include "attn_common.cuh"
 #include "sm100.cuh"
 
@@ -112,6 +112,19 @@ __device__ __forceinline__ Item decode(const AttnArgs& a, const int32_t* rowptr,
   it.e0 = rowptr[r];
   it.n = rowptr[r + 1] - it.e0;
   return it;
+}
+
+// Entry i of an item's list for a whole warp.  The list is read 32 entries at a time into lane
+// registers (lane j holds entry base + j) and handed out with a shuffle, so walking the list
+// costs no dependent global load per entry.  i must be visited in increasing order.
+__device__ __forceinline__ int32_t entry_at(const int32_t* entries, const Item& w, int i, int32_t& held,
+                                            int& base) {
+  if (i >= base + 32) {
+    base = i & ~31;
+    const int j = base + (int)(threadIdx.x & 31);
+    held = j < w.n ? entries[w.e0 + j] : 0;
+  }
+  return __shfl_sync(0xffffffffu, held, i - base);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -200,10 +213,10 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         }
         __syncwarp();
         ++qk;
-        int32_t e_next = entries[w.e0];
+        int32_t held = 0;
+        int base = -32;
         for (int i = 0; i < w.n; ++i, ++it) {
-          const int c = e_next & kEntryIdxMask;
-          if (i + 1 < w.n) e_next = entries[w.e0 + i + 1];
+          const int c = entry_at(entries, w, i, held, base) & kEntryIdxMask;
           const int st = it % kStages;
           if (!warp_mbar_wait(&bars->kv_empty[st], ((it / kStages) & 1) ^ 1, abort)) { ok = false; break; }
           if (elect_one()) {
@@ -276,12 +289,15 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const uint64_t qdesc = sw128_desc(smem_u32(smem + kOffQ + (2 * qs + X) * kQBytes), 16, 1024);
         item_first = steps;
         int last_used = -1;
-        for (int i = 0; i < w.n; ++i)
-          if (entries[w.e0 + i] & f_tile) last_used = i;
-        int32_t e_next = entries[w.e0];
+        for (int b0 = 0; b0 < w.n; b0 += 32) {
+          const int j = b0 + lane;
+          const uint32_t own = __ballot_sync(0xffffffffu, j < w.n && (entries[w.e0 + j] & f_tile) != 0);
+          if (own) last_used = b0 + 31 - __clz(own);
+        }
+        int32_t held = 0;
+        int base = -32;
         for (int i = 0; i < w.n && ok; ++i, ++it) {
-          const int32_t e = e_next;
-          if (i + 1 < w.n) e_next = entries[w.e0 + i + 1];
+          const int32_t e = entry_at(entries, w, i, held, base);
           const int st = it % kStages;
           // Pending PVs hold ring stages: before skipping over an entry this tile does not use,
           // issue them all, or a long run of the other tile's entries could wait on those stages.
@@ -357,95 +373,99 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const Item w = decode(a, rowptr, item);
         float m = -INFINITY, l = 0.f;
         int nsteps = 0;
-        int32_t e_next = w.n > 0 ? entries[w.e0] : 0;
-        for (int i = 0; i < w.n; ++i) {
-          const int32_t e = e_next;
-          if (i + 1 < w.n) e_next = entries[w.e0 + i + 1];
-          if (!(e & f_tile)) continue;                 // warp-uniform: the chunk is the other tile's
-          ++nsteps;
-          const uint32_t sb = it % 3;
-          if (!warp_mbar_wait(&s_full[sb], (it / 3) & 1, abort)) { ok = false; break; }
-          tc_fence_after();
-          uint32_t sr[64];
-          XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
-          XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
-          XSAKE_TMEM_WAIT_LD32(sr);
-          XSAKE_TMEM_WAIT_LD32((sr + 32));
-          uint32_t pk[32];
-          if (e & f_active) {
-            float* x = reinterpret_cast<float*>(sr);   // raw scores
-            if (e & f_diag) {                          // warp-uniform: token-level causal cut
-#pragma unroll
-              for (int j = 0; j < 64; ++j)
-                if (j > diag_lim) x[j] = -INFINITY;
-            }
-            // Row max of the raw scores: a depth-4 tree of 3-input maxes.
-            float t1[22];
-#pragma unroll
-            for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
-            t1[21] = x[63];
-            float t2[8];
-#pragma unroll
-            for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
-            t2[7] = t1[21];
-            const float mraw =
-                fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
-            const float mx = mraw * p.scale_log2;       // log2 units (scale > 0)
-            const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
-            if (m == -INFINITY) m = mx;
-            // TMEM loads/stores are warp-collective: the whole warp rescales when any row must.
-            if (__any_sync(0xffffffffu, need)) {
-              // O holds PV of earlier chunks: wait for the last one, then rescale in TMEM.
-              if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
-              tc_fence_after();
-              const float alpha = need ? ex2(m - mx) : 1.0f;
-              uint32_t orow[32];
-#pragma unroll
-              for (int hcol = 0; hcol < 2; ++hcol) {
-                XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
-                XSAKE_TMEM_WAIT_LD32(orow);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
-                XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
+        // This tile's entries of the item, 32 at a time: a ballot marks them and a shuffle hands
+        // each one out (entries of the other tile are never touched).
+        for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
+          const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
+          uint32_t own = __ballot_sync(0xffffffffu, (eb & f_tile) != 0);
+          while (own) {
+            const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
+            own &= own - 1;
+            ++nsteps;
+            const uint32_t sb = it % 3;
+            if (!warp_mbar_wait(&s_full[sb], (it / 3) & 1, abort)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t sr[64];
+            XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
+            XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
+            XSAKE_TMEM_WAIT_LD32(sr);
+            XSAKE_TMEM_WAIT_LD32((sr + 32));
+            uint32_t pk[32];
+            if (e & f_active) {
+              float* x = reinterpret_cast<float*>(sr);   // raw scores
+              if (e & f_diag) {                          // warp-uniform: token-level causal cut
+  #pragma unroll
+                for (int j = 0; j < 64; ++j)
+                  if (j > diag_lim) x[j] = -INFINITY;
               }
-              tmem_wait_st();
-              if (need) {
-                l *= alpha;
-                m = mx;
+              // Row max of the raw scores: a depth-4 tree of 3-input maxes.
+              float t1[22];
+  #pragma unroll
+              for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+              t1[21] = x[63];
+              float t2[8];
+  #pragma unroll
+              for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
+              t2[7] = t1[21];
+              const float mraw =
+                  fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
+              const float mx = mraw * p.scale_log2;       // log2 units (scale > 0)
+              const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
+              if (m == -INFINITY) m = mx;
+              // TMEM loads/stores are warp-collective: the whole warp rescales when any row must.
+              if (__any_sync(0xffffffffu, need)) {
+                // O holds PV of earlier chunks: wait for the last one, then rescale in TMEM.
+                if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
+                tc_fence_after();
+                const float alpha = need ? ex2(m - mx) : 1.0f;
+                uint32_t orow[32];
+  #pragma unroll
+                for (int hcol = 0; hcol < 2; ++hcol) {
+                  XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
+                  XSAKE_TMEM_WAIT_LD32(orow);
+  #pragma unroll
+                  for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
+                  XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
+                }
+                tmem_wait_st();
+                if (need) {
+                  l *= alpha;
+                  m = mx;
+                }
               }
-            }
-            const float msub = (m == -INFINITY) ? 0.f : m;   // no live score yet: every x is -inf
-            // p = 2^(s*scale*log2e - m): one packed FMA per pair; 3 of every 8 pairs go through
-            // the polynomial exp2 on the FMA/ALU pipes, the rest through MUFU ex2.
-            const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
-            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float x0, x1, p0, p1;
-              upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
-              if ((j & 7) < 3) {
-                exp2_poly2(x0, x1, p0, p1);
-              } else {
-                p0 = ex2(x0);
-                p1 = ex2(x1);
+              const float msub = (m == -INFINITY) ? 0.f : m;   // no live score yet: every x is -inf
+              // p = 2^(s*scale*log2e - m): one packed FMA per pair; 2 of every 8 pairs go through
+              // the polynomial exp2 on the FMA/ALU pipes, the rest through MUFU ex2.
+              const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
+              uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float x0, x1, p0, p1;
+                upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
+                if ((j & 7) < 2) {
+                  exp2_poly2(x0, x1, p0, p1);
+                } else {
+                  p0 = ex2(x0);
+                  p1 = ex2(x1);
+                }
+                acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
+                __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+                pk[j] = *reinterpret_cast<uint32_t*>(&pb);
               }
-              acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
-              __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-              pk[j] = *reinterpret_cast<uint32_t*>(&pb);
+              float s0, s1;
+              upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
+              l += s0 + s1;
+            } else {
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) pk[j] = 0u;
             }
-            float s0, s1;
-            upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
-            l += s0 + s1;
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) pk[j] = 0u;
+            // P over the first 32 columns of the S buffer this thread has just read (its own row).
+            XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_full[sb]);
+            ++it;
           }
-          // P over the first 32 columns of the S buffer this thread has just read (its own row).
-          XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(&p_full[sb]);
-          ++it;
         }
         if (!ok) break;
         // ---------------------------------------------------------------- epilogue
