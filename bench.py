@@ -10,7 +10,7 @@ rank runs its own batch of 4 (weak scaling), no collective on the data path; tim
 over ranks of CUDA-event time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl xsake|reference]
-                    [--workload attn|attn_bwd|softmax|layernorm|entropy]
+                    [--workload attn|attn_bwd|calib|softmax|layernorm|entropy]
 
 --impl reference times the CPU reference semantics (the NumPy port of
 sparse_attention_reference, the reference's own CPU path, dense O(S^2)) on a bounded sample
@@ -379,6 +379,32 @@ def run_rowop(args, dist, rank, world, local):
         calls = [lambda: lib.xsake_entropy_rows(p.data_ptr(), 8, 12, 1024, 1024, sums.data_ptr(), ws.data_ptr(),
                                                 ws.numel(), sp())]
         unit, metric = "GB/s", "HADS entropy over materialised P fp32 [8,12,1024,1024] HBM GB/s"
+    elif wl == "calib":
+        # one config-2 calibration batch: B=8 H=12 S=1024 D=64 fp32, q scaled per head, no mask
+        Bc, Hc, Sc, Dc = 8, 12, 1024, 64
+        tau = torch.linspace(0.25, 4.0, Hc, device="cuda")
+        q = torch.randn(Bc, Hc, Sc, Dc, device="cuda") * tau[None, :, None, None]
+        k = torch.randn(Bc, Hc, Sc, Dc, device="cuda")
+        n = C.c_size_t(0)
+        lib.xsake_entropy_qk_workspace_size(Bc, Hc, Sc, C.byref(n))
+        ws = torch.empty(n.value, dtype=torch.uint8, device="cuda")
+        sums = torch.empty(Hc, dtype=torch.float64, device="cuda")
+        nbytes = None
+        calls = [lambda: lib.xsake_entropy_qk(0, q.data_ptr(), k.data_ptr(), Bc, Hc, Sc, Dc, 0.125, sums.data_ptr(),
+                                              ws.data_ptr(), ws.numel(), sp())]
+        # the drop-in path for comparison: materialised weights, then the entropy reduction
+        full = np.ones((1, 16, 16), bool)
+        cm = sa.compile_block_mask(full, Bc, Hc, Sc, 64, False, q.device)
+        dsc = sa._desc(q, k, k, q, cm, 0.125)
+        pw = torch.empty(Bc, Hc, Sc, Sc, device="cuda")
+        n2 = C.c_size_t(0)
+        lib.xsake_entropy_workspace_size(Bc, Hc, Sc, C.byref(n2))
+        ws2 = torch.empty(n2.value, dtype=torch.uint8, device="cuda")
+        def dropin():
+            st = lib.xsake_attn_probs(C.byref(dsc), cm.plan.data_ptr(), q.data_ptr(), k.data_ptr(), pw.data_ptr(), sp())
+            return st or lib.xsake_entropy_rows(pw.data_ptr(), Bc, Hc, Sc, Sc, sums.data_ptr(), ws2.data_ptr(),
+                                                ws2.numel(), sp())
+        unit, metric = "TFLOP/s", "HADS calibration entropy fused from Q,K (fp32, B=8 H=12 S=1024 D=64) TFLOP/s"
     elif wl == "attn_bwd":
         masks = hads_masks()
         # two input sets of 151 MB (q, k, v, o, do bf16 + lse) alternate, so each call reads
@@ -425,8 +451,22 @@ def run_rowop(args, dist, rank, world, local):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / (args.steps * 20)
+    extra = {}
     if wl == "attn_bwd":
         value = n_active(hads_masks(), B) * 10 * D * 64 * 64 / (ms * 1e-3) / 1e12
+    elif wl == "calib":
+        value = 2 * 2 * 8 * 12 * 1024 * 1024 * 64 / (ms * 1e-3) / 1e12
+        for _ in range(3):
+            _lib.check(dropin())
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+        for _ in range(10):
+            _lib.check(dropin())
+        f1.record()
+        torch.cuda.synchronize()
+        extra = {"dropin_ms_per_batch": f0.elapsed_time(f1) / 10, "fused_ms_per_batch": ms,
+                 "dropin": "xsake_attn_probs (403 MB of fp32 weights) + xsake_entropy_rows"}
     else:
         value = nbytes / (ms * 1e-3) / 1e9
     _, hbm, kind = _peaks()
@@ -434,7 +474,14 @@ def run_rowop(args, dist, rank, world, local):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "config": {"workload": wl, "timing": "CUDA graph of 20 calls" if use_graph else "eager"},
             "note": "secondary row; not the headline"}
-    if unit == "GB/s":
+    line.update(extra)
+    if wl == "calib":
+        fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        line["roofline"] = {"bound": "fp32 CUDA cores", "achieved": value, "peak": fp32_peak, "unit": "TFLOP/s",
+                            "frac": value / fp32_peak,
+                            "peak_source": "nominal fp32 FMA rate (148 SMs x 128 lanes x 2 x 1.965 GHz); "
+                                           "not in the measured peaks"}
+    elif unit == "GB/s":
         line["roofline"] = {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s", "frac": value / hbm,
                             "peak_source": f"hbm_gbs ({kind})"}
     else:
@@ -451,7 +498,7 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="xsake", choices=["xsake", "reference"])
-    ap.add_argument("--workload", default="attn", choices=["attn", "attn_bwd", "softmax", "layernorm", "entropy"])
+    ap.add_argument("--workload", default="attn", choices=["attn", "attn_bwd", "calib", "softmax", "layernorm", "entropy"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -111,6 +111,14 @@ XSAKE_API int xsake_attn_bwd(const XsakeAttnDesc* desc, const void* plan_dev, co
                    const float* lse_dev, const void* do_dev, void* dq_dev, void* dk_dev,
                    void* dv_dev, void* workspace_dev, size_t workspace_bytes, void* stream);
 
+/* The attention weights, the second output of sparse_attention_reference (:45-91) that the
+ * reference's calibration collects (training/trainer.py:79-117): p_dev (fp32, 16-byte aligned)
+ * receives P[b, h, q, k] = softmax over all S keys of q.k * scale with masked entries at
+ * finfo(float32).min, i.e. a fully masked row is uniform 1/S.  head_dim 32 or 64, fp32 or bf16
+ * q/k through desc's strides; uses the plan's mask.  fp32 CUDA-core arithmetic. */
+XSAKE_API int xsake_attn_probs(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
+                   const void* k_dev, float* p_dev, void* stream);
+
 /* ------------------------------------------------------------------ row kernels
  * fused_softmax / fused_softmax_pallas / _softmax_kernel
  * (kernels/pallas/fused_softmax.py:26-87): softmax over the last axis of a contiguous
@@ -144,6 +152,17 @@ XSAKE_API int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t head
                        int64_t sk, double* head_sums_dev, void* workspace_dev,
                        size_t workspace_bytes, void* stream);
 
+/* compute_attention_entropy of softmax(Q K^T * scale) without materialising P: q, k contiguous
+ * [B, H, S, D] (fp32 or bf16, D 32 or 64), no mask (the calibration pass attends fully,
+ * hads_pattern.py:118-166 via training/trainer.py:79-117); scale <= 0 selects 1/sqrt(D).
+ * head_sums_dev[h] = sum over (b, q) of the clipped row entropy, as xsake_entropy_rows gives for
+ * the materialised P.  fp32 scores on the CUDA cores; deterministic. */
+XSAKE_API int xsake_entropy_qk_workspace_size(int64_t batch, int64_t heads, int64_t seq, size_t* bytes);
+XSAKE_API int xsake_entropy_qk(int32_t dtype, const void* q_dev, const void* k_dev, int64_t batch,
+                       int64_t heads, int64_t seq, int64_t head_dim, float scale,
+                       double* head_sums_dev, void* workspace_dev, size_t workspace_bytes,
+                       void* stream);
+
 /* Same result as xsake_entropy_rows for callers that can neither pass a workspace nor allocate
  * device memory (a framework plugin that may only use its framework's allocator, a process
  * whose device memory is all held by a pool allocator, a loop that cannot afford cudaMalloc's
@@ -155,6 +174,20 @@ XSAKE_API int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t head
  * before any stream capture.  All calls share the array, so calls overlapping on the GPU race. */
 XSAKE_API int xsake_entropy_rows_noalloc(const float* p_dev, int64_t batch, int64_t heads,
                        int64_t sq, int64_t sk, double* head_sums_dev, void* stream);
+
+/* ------------------------------------------------------------------ calibration exchange
+ * The single collective of the path: a float64 sum all-reduce of the per-head entropy sums
+ * (xsake_entropy_rows output) across ranks, so every rank builds the same masks.  Replaces the
+ * reference's cross-device reduction (jax.lax.pmean, distributed/pmap_trainer.py:54-55) for
+ * calibration (training/trainer.py:79-117), for callers without torch.distributed.  NCCL is
+ * loaded at run time (libnccl.so.2); without it these calls return XSAKE_EUNSUPPORTED.
+ * Rank 0 calls xsake_comm_unique_id and hands the 128 bytes to every rank out of band; each
+ * rank then calls xsake_comm_init with the CUDA device it will use current. */
+XSAKE_API int xsake_comm_unique_id(uint8_t id_out[128]);
+XSAKE_API int xsake_comm_init(const uint8_t id[128], int nranks, int rank, void** comm_out);
+/* In place on buf_dev (count doubles), stream-ordered on `stream`. */
+XSAKE_API int xsake_comm_allreduce_sum_f64(void* comm, double* buf_dev, size_t count, void* stream);
+XSAKE_API int xsake_comm_destroy(void* comm);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,117 @@
+"""GPU parity of the calibration-side kernels against the NumPy oracle:
+
+* attention weights (the second output of sparse_attention_reference, which the reference's
+  calibration collects): fp32 max|P - ref| <= 1e-5 (weights are <= 1);
+* fused QK -> entropy (compute_attention_entropy of softmax(q k^T * scale) without
+  materialising P): |H - ref| / |ref| <= 1e-5 per head, against the oracle and against the
+  drop-in path (materialised weights + xsake_entropy_rows).
+"""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+from oracle import attention as oa  # noqa: E402
+from oracle import hads as oh  # noqa: E402
+from oracle import inputs as oi  # noqa: E402
+
+P_TOL = 1e-5
+ENT_RTOL = 1e-5
+
+
+def _rand(shape, seed):
+    return np.random.default_rng(seed).standard_normal(shape).astype(np.float32)
+
+
+def _probs_case(B, H, S, D, bs, causal, mask, seed, dtype=np.float32, scale=None):
+    from xsake_b200 import sparse_attention as sa
+    q, k = _rand((B, H, S, D), seed), _rand((B, H, S, D), seed + 1)
+    if dtype != np.float32:
+        q, k = (oi.to_bf16(x).astype(np.float32) for x in (q, k))
+    tq, tk = (torch.from_numpy(x).cuda() for x in (q, k))
+    if dtype != np.float32:
+        tq, tk = tq.to(torch.bfloat16), tk.to(torch.bfloat16)
+    p = sa.attention_probabilities(tq, tk, mask, bs, scale, causal).cpu().numpy()
+    _, ref = oa.sparse_attention_reference(q, k, k, mask, bs, scale=scale, causal=causal)
+    assert p.shape == ref.shape
+    assert np.abs(p - ref).max() <= P_TOL, np.abs(p - ref).max()
+    np.testing.assert_allclose(p.sum(-1), 1.0, atol=1e-5)
+    return p
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_probs_hads_masks(causal):
+    prof = oh.dummy_hads_profile(3, 256, 64, causal=causal, global_blocks=1)
+    _probs_case(2, 3, 256, 64, 64, causal, prof.block_masks, seed=500)
+
+
+def test_probs_fully_masked_rows_are_uniform():
+    m = oh.dummy_hads_profile(2, 192, 64, causal=True).block_masks.copy()
+    m[1, 1, :] = False
+    p = _probs_case(1, 2, 192, 64, 64, True, m, seed=510)
+    np.testing.assert_allclose(p[0, 1, 64:128], 1.0 / 192, rtol=1e-6)
+
+
+def test_probs_batch_mask_head_dim_32_and_bf16():
+    m = np.random.default_rng(3).random((2, 3, 8, 8)) < 0.5
+    m[..., np.arange(8), np.arange(8)] = True
+    _probs_case(2, 3, 256, 32, 32, True, m, seed=520)
+    prof = oh.dummy_hads_profile(2, 128, 64, causal=False)
+    _probs_case(1, 2, 128, 64, 64, False, prof.block_masks, seed=530, dtype="bf16", scale=0.3)
+
+
+def test_sparse_attention_use_pallas_false_returns_weights():
+    from xsake_b200 import sparse_attention as sa
+    prof = oh.dummy_hads_profile(2, 256, 64, causal=True)
+    q, k, v = oi.qkv(1, 2, 256, 64, seed=540)
+    out, w = sa.sparse_attention(q, k, v, prof.block_masks, block_size=64, causal=True, use_pallas=False)
+    ref_o, ref_w = oa.sparse_attention_reference(q, k, v, prof.block_masks, 64, causal=True)
+    assert isinstance(w, np.ndarray) and w.dtype == np.float32
+    assert np.abs(w - ref_w).max() <= P_TOL
+    assert np.abs(out - ref_o).max() <= 1e-5 * max(1.0, np.abs(ref_o).max())
+    out2, none = sa.sparse_attention(q, k, v, prof.block_masks, block_size=64, causal=True)
+    assert none is None
+
+
+def _softmax64(q, k, scale):
+    s = np.einsum("bhqd,bhkd->bhqk", q.astype(np.float64), k.astype(np.float64)) * scale
+    p = np.exp(s - s.max(-1, keepdims=True))
+    return p / p.sum(-1, keepdims=True)
+
+
+@pytest.mark.parametrize("S", [1024, 200, 48])
+def test_entropy_qk_matches_oracle(S):
+    from xsake_b200 import hads_pattern as hp
+    q, k, _ = oi.qkv(2, 12, S, 64, seed=550)
+    got = hp.compute_attention_entropy_qk(q, k, 0.125)
+    ref = oh.compute_attention_entropy(_softmax64(q, k, 0.125))
+    assert got.dtype == np.float32 and got.shape == (12,)
+    assert np.max(np.abs(got - ref) / np.abs(ref)) <= ENT_RTOL, np.max(np.abs(got - ref) / np.abs(ref))
+
+
+def test_entropy_qk_matches_materialised_path_on_calibration_batch():
+    """Config 2's calibration batch shape (B=8, H=12, S=1024, D=64, fp32, q scaled by tau):
+    fused entropies == drop-in path (weights, then xsake_entropy_rows) == oracle on 2 batches."""
+    from xsake_b200 import hads_pattern as hp, sparse_attention as sa
+    q, k = oi.calibration_batch(0)
+    tq, tk = torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda()
+    fused = hp.entropy_head_sums_qk(tq, tk, 0.125).cpu().numpy()
+    full = np.ones((1, 16, 16), bool)
+    w = sa.attention_probabilities(tq, tk, full, 64, 0.125, False)
+    dropin = hp.entropy_head_sums(w).cpu().numpy()
+    np.testing.assert_allclose(fused, dropin, rtol=ENT_RTOL)
+    ref = oh.compute_attention_entropy(_softmax64(q[:2], k[:2], 0.125))
+    got = hp.compute_attention_entropy_qk(tq[:2], tk[:2], 0.125).cpu().numpy()
+    assert np.max(np.abs(got - ref) / np.abs(ref)) <= ENT_RTOL
+
+
+def test_entropy_qk_rejects_bad_arguments():
+    from xsake_b200 import hads_pattern as hp
+    q = torch.zeros(1, 2, 64, 64, device="cuda")
+    with pytest.raises(ValueError):
+        hp.entropy_head_sums_qk(q, torch.zeros(1, 2, 32, 64, device="cuda"))
+    with pytest.raises(Exception):
+        hp.entropy_head_sums_qk(torch.zeros(1, 2, 64, 48, device="cuda"), torch.zeros(1, 2, 64, 48, device="cuda"))

@@ -37,13 +37,18 @@ def calibrate(batch_attn: Callable[[int], torch.Tensor], n_batches: int, seq_len
               min_sparsity: float = 0.10, max_sparsity: float = 0.90, window_size: int = 2,
               causal: bool = True, global_blocks: int = 0,
               head_sums: Callable[[torch.Tensor], torch.Tensor] = hp.entropy_head_sums,
-              group: Optional[object] = None, device=None) -> hp.HADSProfile:
+              group: Optional[object] = None, device=None, comm=None) -> hp.HADSProfile:
     """Build a HADS profile from ``n_batches`` calibration batches split over the ranks of
     ``group`` (or a single process).  ``batch_attn(i)`` returns the attention weights
-    [B, H, Sq, Sk] of batch i; ``head_sums`` reduces them to float64 per-head entropy sums."""
+    [B, H, Sq, Sk] of batch i; ``head_sums`` reduces them to float64 per-head entropy sums.
+    With ``comm`` (an ``xsake_b200.comm.Comm``) the exchange runs through the library's NCCL
+    entry points instead of torch.distributed."""
     dist = _dist()
-    world = dist.get_world_size(group) if dist else 1
-    rank = dist.get_rank(group) if dist else 0
+    if comm is not None:
+        world, rank = comm.nranks, comm.rank
+    else:
+        world = dist.get_world_size(group) if dist else 1
+        rank = dist.get_rank(group) if dist else 0
     sums, rows = None, 0
     for i in local_batches(n_batches, world, rank):
         p = batch_attn(i)
@@ -55,8 +60,11 @@ def calibrate(batch_attn: Callable[[int], torch.Tensor], n_batches: int, seq_len
     if device is not None:
         sums = sums.to(device)
     total = torch.tensor([float(rows)], dtype=torch.float64, device=sums.device)
-    sums = hp.allreduce_head_sums(sums, group)
-    total = hp.allreduce_head_sums(total, group)
+    if comm is not None:
+        sums, total = comm.allreduce_sum_f64(sums.contiguous()), comm.allreduce_sum_f64(total)
+    else:
+        sums = hp.allreduce_head_sums(sums, group)
+        total = hp.allreduce_head_sums(total, group)
     ent = (sums / total).to(torch.float32).cpu().numpy()
     return hp.profile_from_entropies(ent, seq_len, block_size, min_sparsity, max_sparsity, window_size,
                                      causal, global_blocks)

@@ -60,6 +60,37 @@ def entropy_head_sums(attn_weights) -> torch.Tensor:
     return sums
 
 
+def entropy_head_sums_qk(q, k, scale: Optional[float] = None) -> torch.Tensor:
+    """float64 [H] sums over (batch, query) of the row entropies of softmax(q k^T * scale),
+    without materialising the weights (fused on the GPU; q, k [B, H, S, D], fp32 or bf16)."""
+    dev.require_cuda()
+    q, _ = dev.to_device(q)
+    k, _ = dev.to_device(k)
+    q, k = q.contiguous(), k.contiguous()
+    if q.dim() != 4 or k.shape != q.shape or k.dtype != q.dtype:
+        raise ValueError(f"q and k must be [batch, heads, seq, d_head] of one dtype, got {tuple(q.shape)} "
+                         f"{tuple(k.shape)}")
+    B, H, S, D = q.shape
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    _lib.check(lib.xsake_entropy_qk_workspace_size(B, H, S, C.byref(n)))
+    ws = dev.workspace(n.value, q.device)
+    sums = torch.empty(H, dtype=torch.float64, device=q.device)
+    _lib.check(lib.xsake_entropy_qk(dev.xsake_dtype(q), q.data_ptr(), k.data_ptr(), B, H, S, D,
+                                    float(scale) if scale else 0.0, sums.data_ptr(), ws.data_ptr(), ws.numel(),
+                                    dev.stream_ptr()))
+    return sums
+
+
+def compute_attention_entropy_qk(q, k, scale: Optional[float] = None):
+    """``compute_attention_entropy(softmax(q k^T * scale))`` (hads_pattern.py:36-50) fused: the
+    calibration pass's entropies straight from q and k.  float32 [H] (NumPy for host input)."""
+    was_host = not (isinstance(q, torch.Tensor) and q.is_cuda)
+    B, _, S, _ = q.shape
+    ent = (entropy_head_sums_qk(q, k, scale) / float(B * S)).to(torch.float32)
+    return dev.to_host(ent) if was_host else ent
+
+
 def compute_attention_entropy(attn_weights):
     """Mean Shannon entropy per head of softmax weights [B, H, Sq, Sk] (hads_pattern.py:36-50).
     Returns float32 [H]: NumPy for host input, a CUDA tensor for device input."""

@@ -275,14 +275,35 @@ def sparse_attention_pallas(q, k, v, block_mask, block_q: int = 128, block_k: in
     return _finish(out, was_host)
 
 
+def attention_probabilities(q, k, block_mask, block_size: int = 128, scale: Optional[float] = None,
+                            causal: bool = False):
+    """The attention weights of ``sparse_attention_reference`` (sparse_attention.py:45-91):
+    fp32 [B, H, S, S] softmax over all S keys of ``q k^T * scale`` with masked entries at
+    finfo(float32).min (a fully masked row is uniform).  Computed on the GPU (fp32 CUDA-core
+    scores); NumPy in, NumPy out, CUDA tensor in, CUDA tensor out."""
+    was_host = not (isinstance(q, torch.Tensor) and q.is_cuda)
+    q, k = (_unit_last(dev.to_device(t)[0]) for t in (q, k))
+    if q.dim() != 4 or k.shape != q.shape or k.dtype != q.dtype:
+        raise ValueError(f"q and k must be [batch, heads, seq, d_head] of one dtype, got {tuple(q.shape)} "
+                         f"{tuple(k.shape)}")
+    B, H, S, D = q.shape
+    cm = compile_block_mask(block_mask, B, H, S, block_size, causal, q.device)
+    p = torch.empty((B, H, S, S), dtype=torch.float32, device=q.device)
+    d = _desc(q, k, k, q, cm, scale)
+    _lib.check(_lib.load().xsake_attn_probs(C.byref(d), cm.plan.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                            p.data_ptr(), dev.stream_ptr()))
+    return dev.to_host(p) if was_host else p
+
+
 def sparse_attention(q, k, v, block_mask, block_size: int = 128, scale: Optional[float] = None,
                      causal: bool = False, use_pallas: bool = True) -> Tuple[object, Optional[object]]:
-    """Drop-in for sparse_attention.py:257-281.  Always runs the CUDA path and returns
-    ``(out, None)`` like the reference does on GPU; ``use_pallas`` is accepted for signature
-    compatibility (attention weights, the reference CPU path's second output, come from
-    ``xsake_b200.hads_pattern.attention_probabilities``)."""
-    del use_pallas
-    return sparse_attention_pallas(q, k, v, block_mask, block_size, block_size, scale, causal), None
+    """Drop-in for sparse_attention.py:257-281.  ``use_pallas=True`` returns ``(out, None)`` as
+    the reference does on GPU; ``use_pallas=False`` also returns the attention weights, the
+    second output of the reference CPU path (``attention_probabilities``).  Both run on the GPU."""
+    out = sparse_attention_pallas(q, k, v, block_mask, block_size, block_size, scale, causal)
+    if use_pallas:
+        return out, None
+    return out, attention_probabilities(q, k, block_mask, block_size, scale, causal)
 
 
 def broadcast_mask(block_mask, batch: int, heads: int, nb: int):
