@@ -213,9 +213,14 @@ def run_reference(args):
             "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "hads_attn_fwd_cpu_reference", "batch_per_rank": B, "heads": H, "seq_len": S,
-                       "head_dim": D, "block": BS,
-                       "step": "128 query rows x 4096 keys of one head, dense float32 (reference CPU path)"},
+            "config": {"workload": "hads_attn_fwd_bf16_B4_H12_S4096_D64_block64", "batch_per_rank": B,
+                       "heads": H, "seq_len": S, "head_dim": D, "block": BS,
+                       "mask": "dummy_hads_profile rho 0.1-0.9, window 2, causal, global block 0",
+                       "active_blocks_per_rank": n_active(masks, B),
+                       "flops_per_step_per_rank": n_active(masks, B) * FLOP_PER_BLOCK,
+                       "parallelism": "reference CPU path on the host cores of rank 0",
+                       "step": "128 query rows x 4096 keys of one head, dense float32 (reference CPU path); "
+                               "value counts the active-block FLOPs of those rows"},
             "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
                              "sample": f"{args.steps} tiles of 128 query rows x 4096 keys, dense float32 "
                                        "NumPy port of sparse_attention_reference"},
