@@ -807,7 +807,11 @@ cudaError_t g_attr_err[kMaxDev];
 bool tc_attn_bwd_supported(const AttnArgs& a, int dtype) {
   if (!tc_attn_fwd_supported(a, dtype)) return false;
   auto al = [](const void* ptr) { return ((uintptr_t)ptr & 15) == 0; };
-  return al(a.dout) && al(a.dq) && al(a.dk) && al(a.dv);
+  if (!(al(a.dout) && al(a.dq) && al(a.dk) && al(a.dv))) return false;
+  CUtensorMap m;
+  const bool ok = tc_make_map(&m, a.dout, a.os, a.B, a.H, a.S, 128) == XSAKE_OK;
+  clear_error();
+  return ok;
 }
 
 // Workspace: delta [B*H*S] | ucol [B*H*64] | -lse*log2e [B*H*S] | counters (256 B); each

@@ -571,18 +571,13 @@ int tc_make_map(CUtensorMap* map, const void* base, const int64_t st[3], int B, 
   PFN_cuTensorMapEncodeTiled_v12000 enc;
   int s = get_encoder(&enc);
   if (s) return s;
-  struct Dim { cuuint64_t size; cuuint64_t stride; cuuint32_t box; };
-  Dim d[3] = {{(cuuint64_t)S, (cuuint64_t)st[2] * 2, (cuuint32_t)rows},
-              {(cuuint64_t)H, (cuuint64_t)st[1] * 2, 1},
-              {(cuuint64_t)B, (cuuint64_t)st[0] * 2, 1}};
-  std::stable_sort(d, d + 3, [](const Dim& x, const Dim& y) { return x.stride < y.stride; });
-  cuuint64_t dims[4] = {64, d[0].size, d[1].size, d[2].size};
-  cuuint64_t strides[3] = {d[0].stride, d[1].stride, d[2].stride};
-  cuuint32_t box[4] = {64, d[0].box, d[1].box, d[2].box};
+  // Dimensions (d, s, h, b) in the kernels' coordinate order with the caller's strides, whatever
+  // their order: [B, H, S, D] and the projection layout [B, S, H, D] both load as 64-column
+  // tiles of `rows` consecutive tokens.
+  cuuint64_t dims[4] = {64, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)st[2] * 2, (cuuint64_t)st[1] * 2, (cuuint64_t)st[0] * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)rows, 1, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
-  // The kernel addresses tiles as (d, s, h, b); only the canonical order is implemented.
-  XSAKE_REQUIRE(d[0].box == (cuuint32_t)rows, XSAKE_EUNSUPPORTED,
-                "the sequence stride must be the smallest of the (b, h, s) strides");
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -593,10 +588,16 @@ int tc_make_map(CUtensorMap* map, const void* base, const int64_t st[3], int B, 
 bool tc_attn_fwd_supported(const AttnArgs& a, int dtype) {
   if (dtype != XSAKE_BF16 || a.D != 64 || !a.L.has_csr) return false;
   auto aligned = [](const void* ptr, const int64_t* st) {
-    return ((uintptr_t)ptr & 15) == 0 && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0 &&
-           st[2] > 0 && st[2] <= st[1] && st[2] <= st[0];
+    return ((uintptr_t)ptr & 15) == 0 && st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0;
   };
-  return aligned(a.q, a.qs) && aligned(a.k, a.ks) && aligned(a.v, a.vs) && aligned(a.o, a.os);
+  if (!(aligned(a.q, a.qs) && aligned(a.k, a.ks) && aligned(a.v, a.vs) && aligned(a.o, a.os))) return false;
+  // Layouts the TMA unit accepts are taken; anything it rejects goes to the CUDA-core kernels.
+  CUtensorMap m;
+  const bool ok = tc_make_map(&m, a.q, a.qs, a.B, a.H, a.S, 128) == XSAKE_OK &&
+                  tc_make_map(&m, a.k, a.ks, a.B, a.H, a.S, 128) == XSAKE_OK &&
+                  tc_make_map(&m, a.v, a.vs, a.B, a.H, a.S, 128) == XSAKE_OK;
+  clear_error();
+  return ok;
 }
 
 // The work-item counter of the persistent scheduler.

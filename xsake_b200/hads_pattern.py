@@ -208,6 +208,26 @@ def profile_summary(profile: HADSProfile) -> dict:
     }
 
 
+# ----------------------------------------------------------------------------- persistence
+def save_profile(profile: HADSProfile, path) -> None:
+    """Write a calibrated profile (entropies, rho, masks) with the NumPy version that drew the
+    masks; the reference keeps its profile in memory only (training/checkpointing.py:9)."""
+    np.savez(path, head_entropies=np.asarray(profile.head_entropies, np.float32),
+             head_sparsity=np.asarray(profile.head_sparsity, np.float32),
+             block_masks=np.asarray(profile.block_masks, bool), numpy_version=np.array(np.__version__))
+
+
+def load_profile(path) -> HADSProfile:
+    """Read a profile written by ``save_profile``.  The stored masks are used as they are, so a
+    different NumPy version (whose Generator.choice stream may differ) does not change them."""
+    z = np.load(path, allow_pickle=False)
+    for key in ("head_entropies", "head_sparsity", "block_masks"):
+        if key not in z.files:
+            raise ValueError(f"{path}: not a HADS profile (missing {key})")
+    return HADSProfile(z["head_entropies"].astype(np.float32), z["head_sparsity"].astype(np.float32),
+                       z["block_masks"].astype(bool))
+
+
 # ----------------------------------------------------------------------------- multi-rank
 def allreduce_head_sums(sums: torch.Tensor, group: Optional[object] = None) -> torch.Tensor:
     """Sum per-head entropy partials over ranks (each rank's disjoint share of the calibration

@@ -191,7 +191,7 @@ def attention_forward(q, k, v, block_mask, block_size: int = 128, scale: Optiona
     _check_qkv(q, k, v)
     B, H, S, D = q.shape
     cm = compile_block_mask(block_mask, B, H, S, block_size, causal, q.device)
-    o = torch.empty((B, H, S, D), dtype=q.dtype, device=q.device)
+    o = torch.empty_like(q)   # q's layout: a [B, S, H, D] view stays one, with no transpose copy
     lse = torch.empty((B, H, S), dtype=torch.float32, device=q.device)
     d = _desc(q, k, v, o, cm, scale)
     lib = _lib.load()
@@ -212,14 +212,16 @@ def attention_backward(q, k, v, o, lse, dout, block_mask, block_size: int = 128,
     lse = dev.to_device(lse, torch.float32)[0].contiguous()
     _check_qkv(q, k, v)
     B, H, S, D = q.shape
-    if o.stride() != dout.stride():
-        o, dout = o.contiguous(), dout.contiguous()
     cm = compile_block_mask(block_mask, B, H, S, block_size, causal, q.device)
-    dq = torch.empty((B, H, S, D), dtype=q.dtype, device=q.device)
-    dk = torch.empty_like(dq)
-    dv = torch.empty_like(dq)
-    if tuple(o.stride()) != tuple(dq.stride()):
-        o, dout = o.contiguous(), dout.contiguous()
+    # o, dout, dq, dk, dv share one set of strides (the descriptor's o_stride): o's layout, when
+    # o is dense (a strided view such as [B, S, H, D] memory seen as [B, H, S, D]), else packed
+    if tuple(torch.empty_like(o).stride()) != tuple(o.stride()):
+        o = o.contiguous()
+    if tuple(dout.stride()) != tuple(o.stride()):
+        dout = torch.empty_like(o).copy_(dout)
+    dq = torch.empty_like(o)
+    dk = torch.empty_like(o)
+    dv = torch.empty_like(o)
     d = _desc(q, k, v, dq, cm, scale)
     lib = _lib.load()
     ws_n = C.c_size_t(0)
