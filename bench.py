@@ -10,7 +10,7 @@ rank runs its own batch of 4 (weak scaling), no collective on the data path; tim
 over ranks of CUDA-event time.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl xsake|reference]
-                    [--workload attn|attn_bwd|calib|softmax|layernorm|entropy]
+                    [--workload attn|attn_bwd|calib|train|softmax|layernorm|entropy]
 
 --impl reference times the CPU reference semantics (the NumPy port of
 sparse_attention_reference, the reference's own CPU path, dense O(S^2)) on a bounded sample
@@ -344,6 +344,74 @@ def run_attention(args, dist, rank, world, local):
         print(json.dumps(line), flush=True)
 
 
+def run_train(args, dist, rank, world, local):
+    """The config-4 training step (a "next" row, not the headline): 12-layer, d=768 XSAKE
+    transformer, batch 8 per GPU of uniform random token ids, S=4096, bf16 autocast over fp32
+    master weights, fused AdamW; under torch.distributed.run the gradients are all-reduced by
+    DDP (NCCL, bucketed and overlapped with the backward).  Value: whole-job tokens/s."""
+    import torch
+    from xsake_b200.model import ModelConfig, XSAKETransformer, cross_entropy_loss
+    cfg = ModelConfig(seq_len=4096, block_size=64)
+    torch.manual_seed(1234 + rank)
+    model = XSAKETransformer(cfg, device="cuda")
+    if dist is not None:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=64)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    Bt, St = 8, cfg.seq_len
+    batches = [torch.randint(0, cfg.vocab_size, (Bt, St), device="cuda") for _ in range(2)]
+    host = [torch.randint(0, cfg.vocab_size, (Bt, St)).pin_memory() for _ in range(2)]
+
+    def step(ids):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, _ = model(ids)
+            loss = cross_entropy_loss(logits, ids)
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for i in range(args.warmup):
+        step(batches[i % 2])
+    torch.cuda.synchronize()
+    _barrier(dist)
+    clocks = ClockSampler(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        loss = step(batches[i % 2])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), dist) / args.steps
+    # end to end: token ids copied from pinned host memory and the loss read back every step
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(2, args.steps // 2)
+    _barrier(dist)
+    f0.record()
+    for i in range(n_e2e):
+        ids = host[i % 2].to("cuda", non_blocking=True)
+        lv = float(step(ids).detach().cpu())
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(f0.elapsed_time(f1), dist) / n_e2e
+    ck = clocks.stop()
+    _barrier(dist)
+    if rank == 0:
+        tokens = world * Bt * St
+        line = {"metric": "XSAKE transformer training tokens/s (12L d768 H12, S=4096, batch 8 per GPU)",
+                "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "train_xsake_12L_d768_S4096", "global_batch": world * Bt, "seq_len": St,
+                           "mask": "uncalibrated HADS profile (dummy_hads_profile), block 64",
+                           "optimizer": "AdamW fused, fp32 master weights", "parallelism": f"dp{world}",
+                           "loss": float(loss.detach().cpu()), "last_e2e_loss": lv},
+                "note": "secondary row; not the headline",
+                "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": Bt * St * 8,
+                        "d2h_bytes_per_step": 4, "steps": n_e2e},
+                "clocks": ck}
+        print(json.dumps(line), flush=True)
+
+
 def run_rowop(args, dist, rank, world, local):
     """Secondary rows (not the headline): softmax / LayerNorm / entropy / attention backward.
 
@@ -503,7 +571,7 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="xsake", choices=["xsake", "reference"])
-    ap.add_argument("--workload", default="attn", choices=["attn", "attn_bwd", "calib", "softmax", "layernorm", "entropy"])
+    ap.add_argument("--workload", default="attn", choices=["attn", "attn_bwd", "calib", "train", "softmax", "layernorm", "entropy"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -515,6 +583,8 @@ def main():
     try:
         if args.workload == "attn":
             run_attention(args, dist, rank, world, local)
+        elif args.workload == "train":
+            run_train(args, dist, rank, world, local)
         else:
             run_rowop(args, dist, rank, world, local)
     finally:
