@@ -362,7 +362,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
       uint64_t* p_full = bars->p_full[X];
       uint64_t* o_done = bars->o_done[X];
       uint64_t* o_free = &bars->o_free[X];
-      uint32_t it = 0;
+      uint32_t it = 0, sb_c = 0, ph_c = 0;   // step count, its S buffer (it % 3) and phase ((it / 3) & 1)
       bool ok = true;
       for (uint32_t k = 0; ok; ++k) {
         const int slot = k & 1;
@@ -382,8 +382,8 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
             own &= own - 1;
             ++nsteps;
-            const uint32_t sb = it % 3;
-            if (!warp_mbar_wait(&s_full[sb], (it / 3) & 1, abort)) { ok = false; break; }
+            const uint32_t sb = sb_c;
+            if (!warp_mbar_wait(&s_full[sb], ph_c, abort)) { ok = false; break; }
             tc_fence_after();
             uint32_t sr[64];
             XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
@@ -394,17 +394,17 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             if (e & f_active) {
               float* x = reinterpret_cast<float*>(sr);   // raw scores
               if (e & f_diag) {                          // warp-uniform: token-level causal cut
-  #pragma unroll
+#pragma unroll
                 for (int j = 0; j < 64; ++j)
                   if (j > diag_lim) x[j] = -INFINITY;
               }
               // Row max of the raw scores: a depth-4 tree of 3-input maxes.
               float t1[22];
-  #pragma unroll
+#pragma unroll
               for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
               t1[21] = x[63];
               float t2[8];
-  #pragma unroll
+#pragma unroll
               for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
               t2[7] = t1[21];
               const float mraw =
@@ -419,11 +419,11 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
                 tc_fence_after();
                 const float alpha = need ? ex2(m - mx) : 1.0f;
                 uint32_t orow[32];
-  #pragma unroll
+#pragma unroll
                 for (int hcol = 0; hcol < 2; ++hcol) {
                   XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
                   XSAKE_TMEM_WAIT_LD32(orow);
-  #pragma unroll
+#pragma unroll
                   for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
                   XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
                 }
@@ -438,7 +438,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
               // the polynomial exp2 on the FMA/ALU pipes, the rest through MUFU ex2.
               const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
               uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-  #pragma unroll
+#pragma unroll
               for (int j = 0; j < 32; ++j) {
                 float x0, x1, p0, p1;
                 upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
@@ -456,7 +456,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
               upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
               l += s0 + s1;
             } else {
-  #pragma unroll
+#pragma unroll
               for (int j = 0; j < 32; ++j) pk[j] = 0u;
             }
             // P over the first 32 columns of the S buffer this thread has just read (its own row).
@@ -465,6 +465,10 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             tc_fence_before();
             mbar_arrive(&p_full[sb]);
             ++it;
+            if (++sb_c == 3) {
+              sb_c = 0;
+              ph_c ^= 1;
+            }
           }
         }
         if (!ok) break;
