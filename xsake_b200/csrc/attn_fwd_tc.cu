@@ -8,24 +8,28 @@
 // (the Pallas kernel ignores `causal`, the reference CPU path applies it, :79-81), and lse is
 // returned.
 //
-// Work item = 256 query rows of one (b, h): tile A = 64-row chunks (4u, 4u+1), tile B =
-// (4u+2, 4u+3).  The item walks the merged, ascending list of 64-key chunks either tile
-// attends; each chunk's K/V tile is loaded once (TMA, SWIZZLE_128B) into a 9-stage ring and
-// used by both tiles when both attend it.  Per tile and chunk: S = Q K^T (tcgen05, M=128 N=64
+// Each CTA (one per SM, persistent) runs two independent tile workers that share only the SM:
+// each takes its own work items (128 query rows = 64-row chunks 2t, 2t+1 of one (b, h)) from a
+// global counter, longest first, and walks the ascending list of 64-key chunks the tile attends
+// through its own 5-stage K/V ring (TMA, SWIZZLE_128B).  Two workers rather than one 256-row
+// item over a merged chunk list: a merged walk made each tile's MMA warp wait on and release the
+// other tile's chunks and kept the two softmax groups in lock-step (their exponential phases
+// collided on MUFU, their waits left it idle together); independent workers drift apart.
+// Chunks two neighbouring tiles share are read from L2 once per tile (K/V of a (b, h) is 1 MB
+// and stays in L2).  Per tile and chunk: S = Q K^T (tcgen05, M=128 N=64
 // K=64, fp32 in TMEM), softmax by one thread per query row straight out of TMEM, P (bf16)
 // written back into TMEM over the first 32 columns of the scores it came from, O += P V
 // (tcgen05 with A read from TMEM, fp32 accumulator resident in TMEM).  Keeping P out of shared
 // memory matters: an M=128 N=64 K=16 MMA with both operands in shared memory reads 6 KB of it
 // and is bound by shared-memory bandwidth (~50 cycles); with A in TMEM it reads 2 KB and runs at
 // the tensor rate (~35 cycles), and the P stores and their proxy fence disappear.
-// Roles (352 threads, one CTA per SM, persistent):
-//   warps 0-3  softmax + epilogue of tile A (thread i owns row i = TMEM lane i)
-//   warps 4-7  softmax + epilogue of tile B
-//   warp 8     scheduler + TMA producer: takes items from a global counter (longest first),
-//              publishes them through a 2-slot ring, loads Q (double-buffered) and K/V
-//   warps 9,10 MMA issuers of tiles A and B (one elected lane each): QK of a tile's chunk i
-//              is queued before its PV of chunk i-1; a ring stage is released once both
-//              warps are done with it
+// Roles (384 threads):
+//   warps 0-3   softmax + epilogue of tile worker 0 (thread i owns row i = TMEM lane i)
+//   warps 4-7   softmax + epilogue of tile worker 1
+//   warps 8,9   scheduler + TMA producer of workers 0, 1: take items from the global counter,
+//               publish them through a 2-slot ring, load Q (double-buffered) and K/V
+//   warps 10,11 MMA issuers of workers 0, 1 (one elected lane each): QK of chunk i is queued
+//               before PV of chunk i-2; a ring stage is released by the PV that read it
 // TMEM: 512 columns; per tile (at 256*tile) three S buffers [0,64) [64,128) [128,192) so QK
 // runs two chunks ahead of the softmax, and O at [192,256).  P of chunk s lives in S buffer s%3;
 // the MMA warp issues QK of chunk s+3 (which overwrites it) only after PV of chunk s, and one
@@ -46,19 +50,21 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kStages = 9;
-constexpr int kThreads = 352;
+constexpr int kStages = 5;                            // K/V ring stages per tile worker
+constexpr int kQSlots = 2;                            // Q buffers per tile worker
+constexpr uint32_t kPvLag = 3;                        // PV(s - kPvLag) is issued with QK(s)
+constexpr int kThreads = 384;
 constexpr int kQBytes = 128 * 64 * 2;
 constexpr int kKBytes = 64 * 64 * 2;
 constexpr int kStageBytes = 2 * kKBytes;
-constexpr int kOffQ = 0;                              // [2 slots][2 tiles]
-constexpr int kOffKV = kOffQ + 4 * kQBytes;           // [kStages] K then V
-constexpr int kOffBar = kOffKV + kStages * kStageBytes;
+constexpr int kOffQ = 0;                              // [2 tiles][kQSlots]
+constexpr int kOffKV = kOffQ + 2 * kQSlots * kQBytes;  // [2 tiles][kStages] K then V
+constexpr int kOffBar = kOffKV + 2 * kStages * kStageBytes;
 
 struct Bars {
-  uint64_t item_full[2], item_empty[2];
-  uint64_t q_full[2], q_empty[2];
-  uint64_t kv_full[kStages], kv_empty[kStages];
+  uint64_t item_full[2][2], item_empty[2][2];   // [tile][slot]
+  uint64_t q_full[2][2], q_empty[2][2];
+  uint64_t kv_full[2][kStages], kv_empty[2][kStages];
   uint64_t s_full[2][3];                 // [tile][S buffer]
   uint64_t p_full[2][3];                 // [tile][S buffer holding P]
   uint64_t o_done[2][2];                 // [tile][PV parity]
@@ -72,7 +78,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kIdescQK = idesc_bf16(128, 64, false);
 constexpr uint32_t kIdescPV = idesc_bf16(128, 64, true);
 constexpr float kRescaleThreshold = 8.0f;             // log2 units
-constexpr int kItemReaders = 2 + 256;                 // both MMA warps + both softmax warpgroups
+constexpr int kItemReaders = 1 + 128;                 // the tile's MMA warp + its softmax warpgroup
 
 struct TcParams {
   AttnArgs a;
@@ -82,6 +88,18 @@ struct TcParams {
 
 __device__ __forceinline__ void fail(volatile int* abort, int detail) {
   if (atomicExch((int*)abort, 1) == 0) record_device_error(DEV_ERR_TIMEOUT, detail);
+}
+
+// Warp-uniform wait for two barrier phases (the second only if `need2`, warp-uniform): both
+// probes go out before either result is used, so two satisfied waits cost about one.
+__device__ __forceinline__ bool warp_mbar_wait2(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2, bool need2,
+                                                volatile int* abort) {
+  const bool r1 = mbar_try_wait(b1, p1);
+  const bool r2 = need2 ? mbar_try_wait(b2, p2) : true;
+  bool ok = true;
+  if (!r1) ok = mbar_wait(b1, p1, abort);
+  if (ok && !r2) ok = mbar_wait(b2, p2, abort);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // Mean over all S rows of V[b, h] for the rare fully-masked rows; one warp, no block sync.
@@ -104,11 +122,11 @@ struct Item {
 __device__ __forceinline__ Item decode(const AttnArgs& a, const int32_t* rowptr, int item) {
   const PlanLayout& L = a.L;
   Item it;
-  it.u = item % L.nquads;
-  const int bh = item / L.nquads;
+  it.u = item % L.npairs;
+  const int bh = item / L.npairs;
   it.b = bh / a.H;
   it.h = bh % a.H;
-  const int r = L.group_of(it.b, it.h) * L.nquads + it.u;
+  const int r = L.group_of(it.b, it.h) * L.npairs + it.u;
   it.e0 = rowptr[r];
   it.n = rowptr[r + 1] - it.e0;
   return it;
@@ -136,7 +154,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
   volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
   volatile int* plan_ok = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
-  volatile int* item_slot = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);   // [2]
+  volatile int* item_slots = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);   // [tile][slot]
   const AttnArgs& a = p.a;
   const PlanLayout& L = a.L;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -146,19 +164,22 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
     *plan_ok = plan_matches(a) && a.plan[H_HAS_CSR] == 1;
     if (!*plan_ok) record_device_error(DEV_ERR_PLAN, 10);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&bars->item_full[s], 1);
-      mbar_init(&bars->item_empty[s], kItemReaders);
-      mbar_init(&bars->q_full[s], 1);
-      mbar_init(&bars->q_empty[s], 2);        // one release per tile's MMA warp
+      for (int t = 0; t < 2; ++t) {
+        mbar_init(&bars->item_full[t][s], 1);
+        mbar_init(&bars->item_empty[t][s], kItemReaders);
+        mbar_init(&bars->q_full[t][s], 1);
+        mbar_init(&bars->q_empty[t][s], 1);
+      }
       mbar_init(&bars->o_free[s], 128);
       for (int b = 0; b < 2; ++b) mbar_init(&bars->o_done[s][b], 1);
       for (int b = 0; b < 3; ++b) mbar_init(&bars->p_full[s][b], 128);
       for (int b = 0; b < 3; ++b) mbar_init(&bars->s_full[s][b], 1);
     }
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 2);       // one release per tile's MMA warp
-    }
+    for (int t = 0; t < 2; ++t)
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(&bars->kv_full[t][s], 1);
+        mbar_init(&bars->kv_empty[t][s], 1);
+      }
     mbar_init(&bars->drain, 2);
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -176,40 +197,41 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int32_t* rowptr = a.plan + L.q_rowptr_off;
-  const int32_t* entries = a.plan + L.q_entries_off;
-  const int32_t* items = a.plan + L.q_items_off;
+  const int32_t* rowptr = a.plan + L.f_rowptr_off;
+  const int32_t* entries = a.plan + L.f_entries_off;
+  const int32_t* items = a.plan + L.f_items_off;
 
   if (*plan_ok) {
-    if (warp == 8) {
+    if (warp == 8 || warp == 9) {
       // ------------------------------------------------------------------ scheduler + TMA
-      // The whole warp runs the (uniform) control flow; one elected lane issues.
+      // One warp per tile (X = warp - 8); the whole warp runs the (uniform) control flow, one
+      // elected lane issues.
+      const int X = warp - 8;
+      volatile int* item_slot = item_slots + 2 * X;
+      uint8_t* kv0 = smem + kOffKV + X * kStages * kStageBytes;
       uint32_t it = 0, qk = 0;
       bool ok = true;
       for (uint32_t k = 0; ok; ++k) {
         const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_empty[slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+        if (!warp_mbar_wait(&bars->item_empty[X][slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
         int idx = 0;
-        if (lane == 0) idx = *abort ? L.nqitems : atomicAdd(p.counter, 1);
+        if (lane == 0) idx = *abort ? L.nitems : atomicAdd(p.counter, 1);
         idx = __shfl_sync(0xffffffffu, idx, 0);
-        const int item = idx < L.nqitems ? items[idx] : -1;
+        const int item = idx < L.nitems ? items[idx] : -1;
         if (elect_one()) {
           item_slot[slot] = item;
-          mbar_arrive(&bars->item_full[slot]);
+          mbar_arrive(&bars->item_full[X][slot]);
         }
         __syncwarp();
         if (item < 0) break;
         const Item w = decode(a, rowptr, item);
         if (w.n == 0) continue;
-        const int qs = qk & 1;
-        if (!warp_mbar_wait(&bars->q_empty[qs], ((qk >> 1) & 1) ^ 1, abort)) { ok = false; break; }
-        const int row0 = 256 * w.u;
-        const bool has_b = row0 + 128 < a.S;
+        const int qs = qk % kQSlots;
+        if (!warp_mbar_wait(&bars->q_empty[X][qs], ((qk / kQSlots) & 1) ^ 1, abort)) { ok = false; break; }
         if (elect_one()) {
-          mbar_arrive_expect_tx(&bars->q_full[qs], has_b ? 2 * kQBytes : kQBytes);
-          tma_load_4d(smem + kOffQ + (2 * qs) * kQBytes, &tmQ, &bars->q_full[qs], 0, row0, w.h, w.b);
-          if (has_b)
-            tma_load_4d(smem + kOffQ + (2 * qs + 1) * kQBytes, &tmQ, &bars->q_full[qs], 0, row0 + 128, w.h, w.b);
+          mbar_arrive_expect_tx(&bars->q_full[X][qs], kQBytes);
+          tma_load_4d(smem + kOffQ + (kQSlots * X + qs) * kQBytes, &tmQ, &bars->q_full[X][qs], 0, 128 * w.u, w.h,
+                      w.b);
         }
         __syncwarp();
         ++qk;
@@ -218,12 +240,12 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         for (int i = 0; i < w.n; ++i, ++it) {
           const int c = entry_at(entries, w, i, held, base) & kEntryIdxMask;
           const int st = it % kStages;
-          if (!warp_mbar_wait(&bars->kv_empty[st], ((it / kStages) & 1) ^ 1, abort)) { ok = false; break; }
+          if (!warp_mbar_wait(&bars->kv_empty[X][st], ((it / kStages) & 1) ^ 1, abort)) { ok = false; break; }
           if (elect_one()) {
-            uint8_t* kbuf = smem + kOffKV + st * kStageBytes;
-            mbar_arrive_expect_tx(&bars->kv_full[st], kStageBytes);
-            tma_load_4d(kbuf, &tmK, &bars->kv_full[st], 0, 64 * c, w.h, w.b);
-            tma_load_4d(kbuf + kKBytes, &tmV, &bars->kv_full[st], 0, 64 * c, w.h, w.b);
+            uint8_t* kbuf = kv0 + st * kStageBytes;
+            mbar_arrive_expect_tx(&bars->kv_full[X][st], kStageBytes);
+            tma_load_4d(kbuf, &tmK, &bars->kv_full[X][st], 0, 64 * c, w.h, w.b);
+            tma_load_4d(kbuf + kKBytes, &tmV, &bars->kv_full[X][st], 0, 64 * c, w.h, w.b);
           }
           __syncwarp();
         }
@@ -233,25 +255,27 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         // Give copies in flight a bounded chance to land before the CTA exits.
         for (int s = 0; s < kStages; ++s) {
           const uint64_t t0 = global_timer_ns();
-          while (!mbar_try_wait(&bars->kv_full[s], 0) && !mbar_try_wait(&bars->kv_full[s], 1) &&
+          while (!mbar_try_wait(&bars->kv_full[X][s], 0) && !mbar_try_wait(&bars->kv_full[X][s], 1) &&
                  global_timer_ns() - t0 < 1000000ull) {
           }
         }
       }
-    } else if (warp == 9 || warp == 10) {
+    } else if (warp == 10 || warp == 11) {
       // ------------------------------------------------------------------ MMA issuers
-      // One warp per tile (X = warp - 9), so the two tiles' MMA streams issue independently.
-      // The whole warp runs the (uniform) control flow; one elected lane issues.  Every entry
-      // of the merged list is visited in order: an entry this tile does not use is released to
-      // the producer at once (after its load landed, so the release cannot run ahead of the
-      // ring).  QK of step s goes into S buffer s%3 once PV(s-3) has been issued (which implies
-      // the softmax has read S(s-3)); PV(s-2) is issued right after QK(s).
-      const int X = warp - 9;
-      const int32_t f_tile = kQuadFlagsA << (kQuadShiftB * X);
+      // One warp per tile worker (X = warp - 10).
+      // The whole warp runs the (uniform) control flow; one elected lane issues.  The entries
+      // of the item are visited in order (the plan lists only chunks the tile attends; an entry
+      // without an active flag would be released unused, after its load landed).  QK of step s
+      // goes into S buffer s%3 once PV(s-3) has been issued (which implies the softmax has read
+      // S(s-3)); PV(s-2) is issued right after QK(s), the item's last ones at its end.
+      const int X = warp - 10;
+      volatile int* item_slot = item_slots + 2 * X;
+      const int32_t f_tile = kEntryFlags;
       const uint32_t tcol = tmem + 256 * X;
-      const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV), 16, 1024);
+      const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV + X * kStages * kStageBytes), 16, 1024);
       uint32_t it = 0, qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
-      int pstage[3] = {0, 0, 0};
+      int pst0 = 0, pst1 = 0, pst2 = 0;   // ring stage of the step in S buffer 0, 1, 2 (registers)
+      auto pstage = [&](uint32_t b) { return b == 0 ? pst0 : (b == 1 ? pst1 : pst2); };
       bool ok = true;
       auto issue_pv = [&]() -> bool {
         const uint32_t s = pvs, pb = s & 1, sbuf = s % 3;
@@ -259,7 +283,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         const bool first = (s == item_first);
         if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
         tc_fence_after();
-        const int st = pstage[sbuf];
+        const int st = pstage(sbuf);
         if (elect_one()) {
           const uint64_t vdesc = kdesc0 + (uint64_t)((st * kStageBytes + kKBytes) >> 4);
 #pragma unroll
@@ -267,7 +291,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             mma_bf16_ts(tcol + 192, tcol + 64 * sbuf + 8 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
                         (first && kk == 0) ? 0u : 1u);
           mma_commit(&bars->o_done[X][pb]);
-          mma_commit(&bars->kv_empty[st]);
+          mma_commit(&bars->kv_empty[X][st]);
         }
         __syncwarp();
         ++pvs;
@@ -275,18 +299,18 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
       };
       for (uint32_t k = 0; ok; ++k) {
         const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_full[slot], (k >> 1) & 1, abort)) { ok = false; break; }
+        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
         const int item = item_slot[slot];
         __syncwarp();
-        if (elect_one()) mbar_arrive(&bars->item_empty[slot]);
+        if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
         __syncwarp();
         if (item < 0) break;
         const Item w = decode(a, rowptr, item);
         if (w.n == 0) continue;
-        const int qs = qk & 1;
-        if (!warp_mbar_wait(&bars->q_full[qs], (qk >> 1) & 1, abort)) { ok = false; break; }
+        const int qs = qk % kQSlots;
+        if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
         ++qk;
-        const uint64_t qdesc = sw128_desc(smem_u32(smem + kOffQ + (2 * qs + X) * kQBytes), 16, 1024);
+        const uint64_t qdesc = sw128_desc(smem_u32(smem + kOffQ + (kQSlots * X + qs) * kQBytes), 16, 1024);
         item_first = steps;
         int last_used = -1;
         for (int b0 = 0; b0 < w.n; b0 += 32) {
@@ -299,39 +323,56 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         for (int i = 0; i < w.n && ok; ++i, ++it) {
           const int32_t e = entry_at(entries, w, i, held, base);
           const int st = it % kStages;
-          // Pending PVs hold ring stages: before skipping over an entry this tile does not use,
-          // issue them all, or a long run of the other tile's entries could wait on those stages.
-          if (!(e & f_tile))
+          if (!(e & f_tile)) {
+            // Pending PVs hold ring stages: issue them before waiting on an entry that is not used.
             while (ok && pvs < steps) ok = issue_pv();
+            if (!ok || !warp_mbar_wait(&bars->kv_full[X][st], (it / kStages) & 1, abort)) { ok = false; break; }
+            if (elect_one()) mbar_arrive(&bars->kv_empty[X][st]);
+            __syncwarp();
+            continue;
+          }
+          // One batch per step: PV(steps - kPvLag) of this item, then QK(steps) (which needs
+          // PV(steps - 3) issued, so kPvLag <= 3), after one combined wait for both operands.
+          while (ok && pvs + kPvLag < steps) ok = issue_pv();
           if (!ok) break;
-          if (!warp_mbar_wait(&bars->kv_full[st], (it / kStages) & 1, abort)) { ok = false; break; }
-          if (e & f_tile) {
-            while (ok && pvs + 3 <= steps) ok = issue_pv();   // S buffer steps%3 must be free
-            if (!ok) break;
-            const uint32_t sb = steps % 3;
-            tc_fence_after();
-            if (elect_one()) {
-              const uint64_t kdesc = kdesc0 + (uint64_t)((st * kStageBytes) >> 4);
+          const bool pv_now = pvs + kPvLag == steps;
+          const uint32_t ps = pvs, psb = ps % 3;
+          const bool pv_first = pv_now && ps == item_first;
+          if (pv_first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) { ok = false; break; }
+          if (!warp_mbar_wait2(&bars->kv_full[X][st], (it / kStages) & 1, &bars->p_full[X][psb], (ps / 3) & 1,
+                               pv_now, abort)) { ok = false; break; }
+          const uint32_t sb = steps % 3;
+          tc_fence_after();
+          if (elect_one()) {
+            if (pv_now) {
+              const int pst = pstage(psb);
+              const uint64_t vdesc = kdesc0 + (uint64_t)((pst * kStageBytes + kKBytes) >> 4);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
-                mma_bf16_ss(tcol + 64 * sb, qdesc + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
-              mma_commit(&bars->s_full[X][sb]);
-              if (i == last_used) mma_commit(&bars->q_empty[qs]);
+                mma_bf16_ts(tcol + 192, tcol + 64 * psb + 8 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
+                            (pv_first && kk == 0) ? 0u : 1u);
+              mma_commit(&bars->o_done[X][ps & 1]);
+              mma_commit(&bars->kv_empty[X][pst]);
             }
-            __syncwarp();
-            pstage[sb] = st;
-            ++steps;
-            if (pvs + 2 < steps && !issue_pv()) { ok = false; break; }   // keep PV two steps behind
-          } else {
-            if (elect_one()) mbar_arrive(&bars->kv_empty[st]);
-            __syncwarp();
+            const uint64_t kdesc = kdesc0 + (uint64_t)((st * kStageBytes) >> 4);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ss(tcol + 64 * sb, qdesc + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
+            mma_commit(&bars->s_full[X][sb]);
+            if (i == last_used) mma_commit(&bars->q_empty[X][qs]);
           }
+          __syncwarp();
+          if (pv_now) ++pvs;
+          pst0 = sb == 0 ? st : pst0;
+          pst1 = sb == 1 ? st : pst1;
+          pst2 = sb == 2 ? st : pst2;
+          ++steps;
         }
         if (!ok) break;
         while (ok && pvs < steps) ok = issue_pv();
         if (!ok) break;
         if (last_used < 0) {           // this tile had nothing in the item: release its Q share
-          if (elect_one()) mbar_arrive(&bars->q_empty[qs]);
+          if (elect_one()) mbar_arrive(&bars->q_empty[X][qs]);
           __syncwarp();
         }
         if (steps > item_first) ++titems;
@@ -353,28 +394,28 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
       const int half = row >> 6;
       const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
       const uint32_t tcol = tmem + 256 * X;
-      const int shift = kQuadShiftB * X;
-      const int32_t f_tile = kQuadFlagsA << shift;
-      const int32_t f_active = (half ? kFlagActive1 : kFlagActive0) << shift;
-      const int32_t f_diag = (half ? kFlagDiag1 : kFlagDiag0) << shift;
+      volatile int* item_slot = item_slots + 2 * X;
+      const int32_t f_tile = kEntryFlags;
+      const int32_t f_active = half ? kFlagActive1 : kFlagActive0;
+      const int32_t f_diag = half ? kFlagDiag1 : kFlagDiag0;
       const int diag_lim = row & 63;
       uint64_t* s_full = bars->s_full[X];
       uint64_t* p_full = bars->p_full[X];
       uint64_t* o_done = bars->o_done[X];
       uint64_t* o_free = &bars->o_free[X];
       uint32_t it = 0, sb_c = 0, ph_c = 0;   // step count, its S buffer (it % 3) and phase ((it / 3) & 1)
+      bool s_ready = false;                  // S of step `it` already seen complete by every lane
       bool ok = true;
       for (uint32_t k = 0; ok; ++k) {
         const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_full[slot], (k >> 1) & 1, abort)) { ok = false; break; }
+        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
         const int item = item_slot[slot];
-        mbar_arrive(&bars->item_empty[slot]);
+        mbar_arrive(&bars->item_empty[X][slot]);
         if (item < 0) break;
         const Item w = decode(a, rowptr, item);
         float m = -INFINITY, l = 0.f;
         int nsteps = 0;
-        // This tile's entries of the item, 32 at a time: a ballot marks them and a shuffle hands
-        // each one out (entries of the other tile are never touched).
+        // The item's entries, 32 at a time: a ballot marks them and a shuffle hands each one out.
         for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
           const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
           uint32_t own = __ballot_sync(0xffffffffu, (eb & f_tile) != 0);
@@ -383,13 +424,18 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
             own &= own - 1;
             ++nsteps;
             const uint32_t sb = sb_c;
-            if (!warp_mbar_wait(&s_full[sb], ph_c, abort)) { ok = false; break; }
+            if (!s_ready && !warp_mbar_wait(&s_full[sb], ph_c, abort)) { ok = false; break; }
             tc_fence_after();
             uint32_t sr[64];
             XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
             XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
+            // Probe the next step's S while the load is in flight (non-blocking; the QKs run
+            // ahead, so it has usually landed): a complete phase seen by every lane saves the
+            // next wait.  The probe has acquire semantics, like the wait it replaces.
+            const bool next_done = mbar_test_wait(&s_full[sb_c == 2 ? 0 : sb_c + 1], sb_c == 2 ? ph_c ^ 1u : ph_c);
             XSAKE_TMEM_WAIT_LD32(sr);
             XSAKE_TMEM_WAIT_LD32((sr + 32));
+            s_ready = __all_sync(0xffffffffu, next_done);
             uint32_t pk[32];
             if (e & f_active) {
               float* x = reinterpret_cast<float*>(sr);   // raw scores
@@ -473,7 +519,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         }
         if (!ok) break;
         // ---------------------------------------------------------------- epilogue
-        const int tok = 256 * w.u + 128 * X + row;
+        const int tok = 128 * w.u + row;
         const bool valid = tok < a.S;
         const bool empty = valid && !(l > 0.f);
         uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + w.b * a.os[0] +
@@ -632,7 +678,7 @@ int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   p.scale_log2 = a.scale * kLog2e;
   p.counter = reinterpret_cast<int*>(ws);
   XSAKE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(int), s));
-  const int grid = std::max(1, std::min(a.L.nqitems, di.sm_count));
+  const int grid = std::max(1, std::min((a.L.nitems + 1) / 2, di.sm_count));
   tc_fwd_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
   return check_launch("tc_fwd_kernel");
 }

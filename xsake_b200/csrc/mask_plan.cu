@@ -46,14 +46,6 @@ __device__ __forceinline__ int32_t bwd_flags(const uint8_t* m, const PlanLayout&
   return f;
 }
 
-// Flags of kv chunk c for forward quad row (g, u): tile A = pair 2u, tile B = pair 2u+1.
-__device__ __forceinline__ int32_t quad_flags(const uint8_t* m, const PlanLayout& L, int g, int u, int c) {
-  int32_t f = 0;
-  if (2 * u < L.npairs) f |= fwd_flags(m, L, g, 2 * u, c);
-  if (2 * u + 1 < L.npairs) f |= fwd_flags(m, L, g, 2 * u + 1, c) << kQuadShiftB;
-  return f;
-}
-
 __global__ void plan_rows_kernel(PlanLayout L, const uint8_t* __restrict__ mask, int32_t* __restrict__ plan) {
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
@@ -82,13 +74,6 @@ __global__ void plan_rows_kernel(PlanLayout L, const uint8_t* __restrict__ mask,
     }
     frow[r + 1] = nf;
     brow[r + 1] = nb;
-  }
-  int32_t* qrow = plan + L.q_rowptr_off;
-  for (int64_t r = tid; r < L.nqrows; r += nthreads) {
-    const int g = (int)(r / L.nquads), u = (int)(r % L.nquads);
-    int nqq = 0;
-    for (int c = 0; c < L.n64; ++c) nqq += quad_flags(mask, L, g, u, c) != 0;
-    qrow[r + 1] = nqq;
   }
 }
 
@@ -173,20 +158,17 @@ __global__ void plan_scan_kernel(PlanLayout L, int32_t* __restrict__ plan) {
   atomicAdd(&s_active, act);
   atomicAdd(&s_empty, emp);
   const int warp = threadIdx.x >> 5;
-  int64_t f_nnz = 0, b_nnz = 0, q_nnz = 0;
+  int64_t f_nnz = 0, b_nnz = 0;
   if (L.has_csr) {
     if (warp == 0) f_nnz = warp_scan_rowptr(plan + L.f_rowptr_off, L.nrows);
     if (warp == 1) b_nnz = warp_scan_rowptr(plan + L.b_rowptr_off, L.nrows);
-    if (warp == 2) q_nnz = warp_scan_rowptr(plan + L.q_rowptr_off, L.nqrows);
     __syncthreads();
     if (warp == 0) order_items(L, plan + L.f_rowptr_off, plan + L.f_items_off, L.nitems, L.npairs, smem);
     if (warp == 1)
       order_items(L, plan + L.b_rowptr_off, plan + L.b_items_off, L.nitems, L.npairs, smem + (L.n64 + 2));
-    if (warp == 2)
-      order_items(L, plan + L.q_rowptr_off, plan + L.q_items_off, L.nqitems, L.nquads, smem + 2 * (L.n64 + 2));
   }
   __syncthreads();
-  if (threadIdx.x == 0 || threadIdx.x == 32 || threadIdx.x == 64) {
+  if (threadIdx.x == 0 || threadIdx.x == 32) {
     int32_t* hdr = plan;
     if (threadIdx.x == 0) {
       hdr[H_VERSION] = kPlanVersion;
@@ -207,13 +189,11 @@ __global__ void plan_scan_kernel(PlanLayout L, int32_t* __restrict__ plan) {
       hdr[H_ACTIVE_LO] = (int32_t)(active & 0xffffffff); hdr[H_ACTIVE_HI] = (int32_t)(active >> 32);
       hdr[H_TILES_LO] = (int32_t)(tiles & 0xffffffff);   hdr[H_TILES_HI] = (int32_t)(tiles >> 32);
       hdr[H_EMPTY_LO] = (int32_t)(empty & 0xffffffff);   hdr[H_EMPTY_HI] = (int32_t)(empty >> 32);
-      hdr[H_ITEMS_LO] = L.has_csr ? L.nqitems : 0;       hdr[H_ITEMS_HI] = 0;
+      hdr[H_ITEMS_LO] = L.has_csr ? L.nitems : 0;        hdr[H_ITEMS_HI] = 0;
       __threadfence();
       hdr[H_MAGIC] = kPlanMagic;
-    } else if (threadIdx.x == 32) {
-      plan[H_B_NNZ] = (int32_t)b_nnz;
     } else {
-      plan[H_Q_NNZ] = (int32_t)q_nnz;
+      plan[H_B_NNZ] = (int32_t)b_nnz;
     }
   }
 }
@@ -226,16 +206,6 @@ __global__ void plan_fill_kernel(PlanLayout L, int32_t* __restrict__ plan) {
   const int32_t* brow = plan + L.b_rowptr_off;
   int32_t* fent = plan + L.f_entries_off;
   int32_t* bent = plan + L.b_entries_off;
-  const int32_t* qrow = plan + L.q_rowptr_off;
-  int32_t* qent = plan + L.q_entries_off;
-  for (int64_t r = tid; r < L.nqrows; r += nthreads) {
-    const int g = (int)(r / L.nquads), u = (int)(r % L.nquads);
-    int32_t pos = qrow[r];
-    for (int c = 0; c < L.n64; ++c) {
-      const int32_t f = quad_flags(m, L, g, u, c);
-      if (f) qent[pos++] = c | f;
-    }
-  }
   for (int64_t r = tid; r < 2 * (int64_t)L.nrows; r += nthreads) {
     const bool fwd = r < L.nrows;
     const int64_t rr = fwd ? r : r - L.nrows;
@@ -298,7 +268,7 @@ extern "C" int xsake_mask_compile(const XsakeMaskDims* dims, const uint8_t* mask
   const int blocks = (int)std::min<int64_t>((work + 255) / 256, 4 * (int64_t)di.sm_count);
   plan_rows_kernel<<<std::max(blocks, 1), 256, 0, s>>>(L, mask_dev, (int32_t*)plan_dev);
   if ((st = check_launch("plan_rows_kernel"))) return st;
-  const size_t smem = 3 * (size_t)(L.n64 + 2) * sizeof(int32_t);
+  const size_t smem = 2 * (size_t)(L.n64 + 2) * sizeof(int32_t);
   XSAKE_REQUIRE(smem <= 48 * 1024, XSAKE_EUNSUPPORTED, "seq too long for the plan compiler");
   plan_scan_kernel<<<1, 1024, smem, s>>>(L, (int32_t*)plan_dev);
   if ((st = check_launch("plan_scan_kernel"))) return st;

@@ -12,10 +12,6 @@
 //   b_rowptr  [nrows + 1]       backward kv-pair columns: (g, u) covers kv chunks 2u, 2u+1;
 //   b_entries [nrows * n64]     each entry is a 64-token q chunk with per-half flags
 //   b_items   [B * H * npairs]  backward work items, longest first
-//   q_rowptr  [nqrows + 1]      forward quad rows: (g, u) covers 256 query rows = two pair tiles
-//   q_entries [nqrows * n64]    A = pair 2u, B = pair 2u+1; each entry is a kv chunk used by A
-//                               and/or B, flags of A in bits 20-23 and of B in bits 24-27
-//   q_items   [B * H * nquads]  quad work items (b*H + h)*nquads + u, longest first
 #pragma once
 
 #include <stdint.h>
@@ -23,7 +19,7 @@
 namespace xsake {
 
 constexpr int32_t kPlanMagic = 0x504B5358;  // "XSKP"
-constexpr int32_t kPlanVersion = 1;
+constexpr int32_t kPlanVersion = 2;
 constexpr int kPlanHeaderWords = 32;
 
 // Entry encoding: low 20 bits = chunk index, then flags.
@@ -32,14 +28,12 @@ constexpr int32_t kFlagActive0 = 1 << 20;  // half 0 (first 64 rows of the tile)
 constexpr int32_t kFlagActive1 = 1 << 21;  // half 1 attends
 constexpr int32_t kFlagDiag0 = 1 << 22;    // half 0 needs the token-level causal test
 constexpr int32_t kFlagDiag1 = 1 << 23;    // half 1 needs the token-level causal test
-constexpr int kQuadShiftB = 4;             // quad entries: tile B's flags = tile A's << 4
-constexpr int32_t kQuadFlagsA = 0xF << 20;
-constexpr int32_t kQuadFlagsB = 0xF << 24;
+constexpr int32_t kEntryFlags = 0xF << 20;  // any of the four flags
 
 // Header word indices.
 enum PlanHeader : int {
   H_MAGIC = 0, H_VERSION, H_B, H_H, H_S, H_BM, H_HM, H_BS, H_CAUSAL, H_HAS_CSR,
-  H_F_NNZ, H_B_NNZ, H_Q_NNZ,
+  H_F_NNZ, H_B_NNZ,
   H_ACTIVE_LO = 16, H_ACTIVE_HI, H_TILES_LO, H_TILES_HI, H_EMPTY_LO, H_EMPTY_HI,
   H_ITEMS_LO, H_ITEMS_HI,
 };
@@ -47,10 +41,9 @@ enum PlanHeader : int {
 struct PlanLayout {
   int32_t B, H, S, Bm, Hm, bs, causal;
   int32_t nq, n64, npairs, nrows, nitems, has_csr;
-  int32_t nquads, nqrows, nqitems;
   int64_t mask_off, qempty_off, f_rowptr_off, f_entries_off, f_items_off;
   int64_t b_rowptr_off, b_entries_off, b_items_off;
-  int64_t q_rowptr_off, q_entries_off, q_items_off, total_words;
+  int64_t total_words;
 
   // Returns false when the dims are invalid.
   __host__ __device__ bool init(int32_t B_, int32_t H_, int32_t S_, int32_t Bm_, int32_t Hm_,
@@ -64,9 +57,6 @@ struct PlanLayout {
     npairs = (n64 + 1) / 2;
     nrows = Bm * Hm * npairs;
     nitems = B * H * npairs;
-    nquads = (npairs + 1) / 2;
-    nqrows = Bm * Hm * nquads;
-    nqitems = B * H * nquads;
     int64_t w = kPlanHeaderWords;
     const int64_t mask_bytes = (int64_t)Bm * Hm * nq * nq;
     mask_off = w;
@@ -80,9 +70,6 @@ struct PlanLayout {
     b_rowptr_off = w;  w += csr * (nrows + 1);
     b_entries_off = w; w += csr * (int64_t)nrows * n64;
     b_items_off = w;   w += csr * nitems;
-    q_rowptr_off = w;  w += csr * (nqrows + 1);
-    q_entries_off = w; w += csr * (int64_t)nqrows * n64;
-    q_items_off = w;   w += csr * nqitems;
     total_words = w;
     return true;
   }
