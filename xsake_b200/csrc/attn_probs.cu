@@ -210,14 +210,25 @@ __global__ void __launch_bounds__(kThreadsP) probs_kernel(ProbsArgs a) {
   }
 }
 
-__global__ void probs_heads_kernel(const double* __restrict__ partial, int B, int H, int per_bh,
-                                   double* __restrict__ head_sums) {
-  const int h = blockIdx.x * blockDim.x + threadIdx.x;
-  if (h >= H) return;
+// One CTA per head: thread t sums partials t, t + 256, ... (in (b, tile) order), then a fixed
+// shared-memory tree; the order depends only on the shapes.
+__global__ void __launch_bounds__(256) probs_heads_kernel(const double* __restrict__ partial, int B, int H,
+                                                          int per_bh, double* __restrict__ head_sums) {
+  __shared__ double red[256];
+  const int h = blockIdx.x;
+  const int64_t n = (int64_t)B * per_bh;
   double acc = 0.0;
-  for (int b = 0; b < B; ++b)
-    for (int c = 0; c < per_bh; ++c) acc += partial[((int64_t)b * H + h) * per_bh + c];
-  head_sums[h] = acc;
+  for (int64_t i = threadIdx.x; i < n; i += 256) {
+    const int64_t b = i / per_bh, c = i - b * per_bh;
+    acc += partial[(b * H + h) * per_bh + c];
+  }
+  red[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if ((int)threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) head_sums[h] = red[0];
 }
 
 template <typename T, bool PROBS>
@@ -309,7 +320,7 @@ extern "C" int xsake_entropy_qk(int32_t dtype, const void* q_dev, const void* k_
   int r = dtype == XSAKE_F32 ? launch<float, false>(a, (int)head_dim, s)
                              : launch<__nv_bfloat16, false>(a, (int)head_dim, s);
   if (r) return r;
-  probs_heads_kernel<<<(unsigned)((heads + 127) / 128), 128, 0, s>>>(a.partial, a.B, a.H,
-                                                                     (a.S + kRows - 1) / kRows, head_sums_dev);
+  probs_heads_kernel<<<(unsigned)heads, 256, 0, s>>>(a.partial, a.B, a.H, (a.S + kRows - 1) / kRows,
+                                                     head_sums_dev);
   return check_launch("probs_heads_kernel");
 }

@@ -77,20 +77,37 @@ __global__ void __launch_bounds__(256) entropy_rows_kernel(const float* __restri
   }
 }
 
-__global__ void entropy_heads_kernel(const double* __restrict__ partial, EntropyGeom g, double* __restrict__ head_sums) {
-  const int h = blockIdx.x * blockDim.x + threadIdx.x;
-  if (h >= g.H) return;
+// One CTA per head: thread t sums partials t, t + 256, ... of the head's B * ctas_per_bh (in
+// (b, chunk) order), then a fixed shared-memory tree; the order depends only on the shapes.
+__global__ void __launch_bounds__(256) entropy_heads_kernel(const double* __restrict__ partial, EntropyGeom g,
+                                                            double* __restrict__ head_sums) {
+  __shared__ double red[256];
+  const int h = blockIdx.x;
+  const int64_t per_b = g.ctas_per_bh, n = g.B * per_b;
   double t = 0.0;
-  for (int64_t b = 0; b < g.B; ++b)
-    for (int64_t c = 0; c < g.ctas_per_bh; ++c) t += partial[(b * g.H + h) * g.ctas_per_bh + c];
-  head_sums[h] = t;
+  for (int64_t i = threadIdx.x; i < n; i += 256) {
+    const int64_t b = i / per_b, c = i - b * per_b;
+    t += partial[(b * g.H + h) * per_b + c];
+  }
+  red[threadIdx.x] = t;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if ((int)threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) head_sums[h] = red[0];
 }
 
+// One wave: as many CTAs as are resident at once (occupancy of this kernel), so no CTA starts
+// after the others have drained and every SM streams until the end.
 unsigned entropy_grid(int64_t nchunks) {
   DeviceInfo di;
   const int sms = device_info(&di) == XSAKE_OK ? di.sm_count : 148;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, entropy_rows_kernel, 256, 0) != cudaSuccess || per_sm < 1)
+    per_sm = 1;
   clear_error();
-  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(nchunks, (int64_t)sms * 8));
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(nchunks, (int64_t)sms * per_sm));
 }
 
 EntropyGeom geom(int64_t B, int64_t H, int64_t Sq, int64_t Sk) {
@@ -134,7 +151,7 @@ extern "C" int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t hea
   entropy_rows_kernel<<<entropy_grid(nctas), 256, 0, s>>>(p_dev, g, nctas, partial);
   int st = check_launch("entropy_rows_kernel");
   if (st) return st;
-  entropy_heads_kernel<<<(unsigned)((heads + 127) / 128), 128, 0, s>>>(partial, g, head_sums_dev);
+  entropy_heads_kernel<<<(unsigned)heads, 256, 0, s>>>(partial, g, head_sums_dev);
   return check_launch("entropy_heads_kernel");
 }
 
@@ -205,6 +222,6 @@ extern "C" int xsake_entropy_rows_noalloc(const float* p_dev, int64_t batch, int
   cudaStream_t s = as_stream(stream);
   entropy_rows_kernel<<<entropy_grid(nctas), 256, 0, s>>>(p_dev, g, nctas, partial);
   if ((st = check_launch("entropy_rows_kernel"))) return st;
-  entropy_heads_kernel<<<(unsigned)((heads + 127) / 128), 128, 0, s>>>(partial, g, head_sums_dev);
+  entropy_heads_kernel<<<(unsigned)heads, 256, 0, s>>>(partial, g, head_sums_dev);
   return check_launch("entropy_heads_kernel");
 }
