@@ -110,6 +110,31 @@ def test_bf16_odd_chunk_count_and_empty_rows():
     _bf16_case(1, 2, 320, 64, 64, True, m, seed=30)
 
 
+def test_bf16_paired_units_odd_count_and_empty_rows():
+    # Masks shared over the batch pair (b, h) units of one head; with three batches the third
+    # runs alone.  S = 320 gives an odd chunk count; one q-block attends nothing.
+    m = oh.dummy_hads_profile(2, 320, 64, causal=True).block_masks.copy()
+    m[1, 2, :] = False
+    m[0, 4, :4] = False
+    _bf16_case(3, 2, 320, 64, 64, True, m, seed=31)
+    _bf16_case(3, 2, 320, 64, 64, False, m, seed=32)
+
+
+def test_bf16_mask_shared_over_heads():
+    # A [B, 1, nq, nk] mask: one mask per batch, shared by the heads (units paired over heads,
+    # three heads so one runs alone).
+    m = np.stack([oh.build_head_mask(0.6, 8, 1, 5 + b, causal=True) for b in range(2)])[:, None]
+    _bf16_case(2, 3, 512, 64, 64, True, m, seed=33)
+
+
+def test_bf16_mask_per_unit():
+    # A mask per (b, h) unit leaves nothing to pair: the query-chunk-pair kernel runs.
+    m = np.stack([oh.dummy_hads_profile(3, 512, 64, causal=True, global_blocks=b).block_masks
+                  for b in range(2)])
+    _bf16_case(2, 3, 512, 64, 64, True, m, seed=34)
+    _bf16_case(2, 3, 512, 64, 64, False, m, seed=35)
+
+
 def test_bf16_bshd_layout_and_scale():
     prof = oh.dummy_hads_profile(4, 256, 64, causal=True)
     _bf16_case(2, 4, 256, 64, 64, True, prof.block_masks, seed=40, layout="bshd", scale=0.2)

@@ -36,6 +36,11 @@
 // thread's MMAs execute in issue order.
 // The running max is only moved when it grows by more than 2^8 (rescaling O in TMEM is then
 // rare); exp2 runs on MUFU for 3/4 of the elements and on a cubic polynomial for the rest.
+//
+// Two kernels share this structure.  tc_fwd_kernel (above) pairs query chunks 2t, 2t+1 of one
+// (b, h) and is used when every (b, h) has its own mask.  tc_fwd_pair_kernel pairs the same
+// query chunk of two (b, h) units that share a mask (a mask broadcast over the batch or the
+// heads, the usual HADS case) and is used whenever two such units exist; see its comment.
 #include "attn_common.cuh"
 #include "sm100.cuh"
 
@@ -135,7 +140,8 @@ __device__ __forceinline__ Item decode(const AttnArgs& a, const int32_t* rowptr,
 // Entry i of an item's list for a whole warp.  The list is read 32 entries at a time into lane
 // registers (lane j holds entry base + j) and handed out with a shuffle, so walking the list
 // costs no dependent global load per entry.  i must be visited in increasing order.
-__device__ __forceinline__ int32_t entry_at(const int32_t* entries, const Item& w, int i, int32_t& held,
+template <class W>
+__device__ __forceinline__ int32_t entry_at(const int32_t* entries, const W& w, int i, int32_t& held,
                                             int& base) {
   if (i >= base + 32) {
     base = i & ~31;
@@ -587,9 +593,520 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Paired-unit forward.  A mask broadcast over the batch (or the heads) gives several (b, h)
+// units the same chunk lists.  A work item of this kernel is one 64-row query chunk j of TWO
+// such units u0, u1: every step is one 64-key chunk c that chunk j attends, computed for both
+// units at once, so both halves of every step do useful work.  The kernel above pairs query
+// chunks 2t and 2t+1 of ONE unit instead and walks the union of their lists; on HADS masks the
+// two lists differ in their random long-range picks and 23% of its half-steps are masked out.
+//
+// The two units' scores and outputs are M=64 accumulators interleaved in TMEM: unit u0's row r
+// sits in lane 32*(r/16) + r%16, unit u1's in the same lane + 16, so each softmax warp holds 16
+// rows of each unit (lanes 0-15: u0, lanes 16-31: u1) and still owns one row per thread.  Per
+// step and unit: S = Q K^T (tcgen05 M=64 N=64, A and B in shared memory), P written back over
+// the first 32 columns of the unit's scores, O += P V (M=64, A read from the same TMEM lanes as
+// the accumulator).  A ring slot holds one unit's K and V chunk; a step takes two consecutive
+// slots (u0's, then u1's).  Roles, barriers, the scheduler, bounded waits and the softmax
+// arithmetic are those of tc_fwd_kernel.  Items are taken in descending j (longest lists first
+// under a causal mask).  With an odd number of units per mask the last unit of each group runs
+// alone: its partner lanes are masked out and its second slot is released without a load.
+struct PItem {
+  int b0, h0, b1, h1, j, e0, n;
+  bool solo;
+};
+
+__host__ __device__ __forceinline__ int pair_units(const PlanLayout& L, int B, int H) {
+  return (L.Bm == 1 ? B : 1) * (L.Hm == 1 ? H : 1);
+}
+__host__ __device__ __forceinline__ int pair_items(const PlanLayout& L, int B, int H) {
+  return L.n64 * L.Bm * L.Hm * ((pair_units(L, B, H) + 1) / 2);
+}
+
+__device__ __forceinline__ PItem decode_pair(const AttnArgs& a, const int32_t* rowptr, int item) {
+  const PlanLayout& L = a.L;
+  const int fh = L.Hm == 1 ? a.H : 1;
+  const int U = pair_units(L, a.B, a.H), P = (U + 1) / 2, per_j = L.Bm * L.Hm * P;
+  PItem it;
+  it.j = L.n64 - 1 - item / per_j;
+  const int rem = item % per_j, g = rem / P, u0 = 2 * (rem % P);
+  it.solo = u0 + 1 >= U;
+  const int u1 = it.solo ? u0 : u0 + 1;
+  const int gb = L.Bm == 1 ? 0 : g / L.Hm, gh = L.Hm == 1 ? 0 : g % L.Hm;
+  it.b0 = L.Bm == 1 ? u0 / fh : gb;
+  it.h0 = L.Hm == 1 ? u0 % fh : gh;
+  it.b1 = L.Bm == 1 ? u1 / fh : gb;
+  it.h1 = L.Hm == 1 ? u1 % fh : gh;
+  const int r = g * L.npairs + (it.j >> 1);
+  it.e0 = rowptr[r];
+  it.n = rowptr[r + 1] - it.e0;
+  return it;
+}
+
+// Number of entries of the list carrying flag f, and the index of the last one (-1 if none).
+__device__ __forceinline__ int count_steps(const int32_t* entries, int e0, int n, int32_t f, int& last) {
+  const int lane = threadIdx.x & 31;
+  int cnt = 0;
+  last = -1;
+  for (int b0 = 0; b0 < n; b0 += 32) {
+    const int j = b0 + lane;
+    const uint32_t own = __ballot_sync(0xffffffffu, j < n && (entries[e0 + j] & f) != 0);
+    cnt += __popc(own);
+    if (own) last = b0 + 31 - __clz(own);
+  }
+  return cnt;
+}
+
+constexpr uint32_t kIdescQK64 = idesc_bf16(64, 64, false);
+constexpr uint32_t kIdescPV64 = idesc_bf16(64, 64, true);
+constexpr uint32_t kLane16 = 16u << 16;   // TMEM address of the partner unit's lanes
+constexpr int kPairKStages = 2;           // K ring (both units' K chunks per stage), released by QK
+constexpr int kPairVStages = 3;           // V ring, released by PV
+static_assert(kPairKStages + kPairVStages <= kStages, "the pair rings reuse the K/V ring's shared memory");
+
+__global__ void __launch_bounds__(kThreads, 1)
+tc_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
+  volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
+  volatile int* plan_ok = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
+  volatile int* item_slots = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);   // [tile][slot]
+  const AttnArgs& a = p.a;
+  const PlanLayout& L = a.L;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nitems = pair_items(L, a.B, a.H);
+
+  if (threadIdx.x == 0) {
+    *abort = 0;
+    *plan_ok = plan_matches(a) && a.plan[H_HAS_CSR] == 1;
+    if (!*plan_ok) record_device_error(DEV_ERR_PLAN, 11);
+    for (int s = 0; s < 2; ++s) {
+      for (int t = 0; t < 2; ++t) {
+        mbar_init(&bars->item_full[t][s], 1);
+        mbar_init(&bars->item_empty[t][s], kItemReaders);
+        mbar_init(&bars->q_full[t][s], 1);
+        mbar_init(&bars->q_empty[t][s], 1);
+      }
+      mbar_init(&bars->o_free[s], 128);
+      for (int b = 0; b < 2; ++b) mbar_init(&bars->o_done[s][b], 1);
+      for (int b = 0; b < 3; ++b) mbar_init(&bars->p_full[s][b], 128);
+      for (int b = 0; b < 3; ++b) mbar_init(&bars->s_full[s][b], 1);
+    }
+    for (int t = 0; t < 2; ++t)
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(&bars->kv_full[t][s], 1);
+        mbar_init(&bars->kv_empty[t][s], 1);
+      }
+    mbar_init(&bars->drain, 2);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int32_t* rowptr = a.plan + L.f_rowptr_off;
+  const int32_t* entries = a.plan + L.f_entries_off;
+
+  if (*plan_ok) {
+    if (warp == 8 || warp == 9) {
+      // ------------------------------------------------------------------ scheduler + TMA
+      const int X = warp - 8;
+      volatile int* item_slot = item_slots + 2 * X;
+      uint8_t* kv0 = smem + kOffKV + X * kStages * kStageBytes;
+      uint32_t it = 0, qk = 0;
+      bool ok = true;
+      for (uint32_t k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!warp_mbar_wait(&bars->item_empty[X][slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+        int idx = 0;
+        if (lane == 0) idx = *abort ? nitems : atomicAdd(p.counter, 1);
+        idx = __shfl_sync(0xffffffffu, idx, 0);
+        const int item = idx < nitems ? idx : -1;
+        if (elect_one()) {
+          item_slot[slot] = item;
+          mbar_arrive(&bars->item_full[X][slot]);
+        }
+        __syncwarp();
+        if (item < 0) break;
+        const PItem w = decode_pair(a, rowptr, item);
+        const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
+        int last = -1;
+        if (count_steps(entries, w.e0, w.n, fa, last) == 0) continue;
+        const int qs = qk % kQSlots;
+        if (!warp_mbar_wait(&bars->q_empty[X][qs], ((qk / kQSlots) & 1) ^ 1, abort)) { ok = false; break; }
+        if (elect_one()) {
+          uint8_t* qbuf = smem + kOffQ + (kQSlots * X + qs) * kQBytes;
+          mbar_arrive_expect_tx(&bars->q_full[X][qs], w.solo ? kQBytes / 2 : kQBytes);
+          tma_load_4d(qbuf, &tmQ, &bars->q_full[X][qs], 0, 64 * w.j, w.h0, w.b0);
+          if (!w.solo) tma_load_4d(qbuf + kQBytes / 2, &tmQ, &bars->q_full[X][qs], 0, 64 * w.j, w.h1, w.b1);
+        }
+        __syncwarp();
+        ++qk;
+        // K of step s goes out before V of step s-1: V(s-1) waits for PV(s-4), which the MMA
+        // warp issues only with QK(s-1), so K is never held up behind a V slot.
+        const uint32_t bytes = w.solo ? kKBytes : 2 * kKBytes;
+        auto load_pair = [&](const CUtensorMap* map, int bar, uint8_t* buf, int c) {
+          if (elect_one()) {
+            mbar_arrive_expect_tx(&bars->kv_full[X][bar], bytes);
+            tma_load_4d(buf, map, &bars->kv_full[X][bar], 0, 64 * c, w.h0, w.b0);
+            if (!w.solo) tma_load_4d(buf + kKBytes, map, &bars->kv_full[X][bar], 0, 64 * c, w.h1, w.b1);
+          }
+          __syncwarp();
+        };
+        auto load_v = [&](uint32_t s, int c) -> bool {
+          const int vs = s % kPairVStages;
+          if (!warp_mbar_wait(&bars->kv_empty[X][kPairKStages + vs], ((s / kPairVStages) & 1) ^ 1, abort))
+            return false;
+          load_pair(&tmV, kPairKStages + vs, kv0 + (kPairKStages + vs) * kStageBytes, c);
+          return true;
+        };
+        int32_t held = 0;
+        int base = -32, pend_c = -1;
+        for (int i = 0; i < w.n && ok; ++i) {
+          const int32_t e = entry_at(entries, w, i, held, base);
+          if (!(e & fa)) continue;
+          const int c = e & kEntryIdxMask;
+          const int ks = it % kPairKStages;
+          if (!warp_mbar_wait(&bars->kv_empty[X][ks], ((it / kPairKStages) & 1) ^ 1, abort)) { ok = false; break; }
+          load_pair(&tmK, ks, kv0 + ks * kStageBytes, c);
+          if (pend_c >= 0 && !load_v(it - 1, pend_c)) { ok = false; break; }
+          pend_c = c;
+          ++it;
+        }
+        if (ok && pend_c >= 0 && !load_v(it - 1, pend_c)) ok = false;
+      }
+      if (!ok && lane == 0) {
+        fail(abort, 1);
+        for (int s = 0; s < kStages; ++s) {
+          const uint64_t t0 = global_timer_ns();
+          while (!mbar_try_wait(&bars->kv_full[X][s], 0) && !mbar_try_wait(&bars->kv_full[X][s], 1) &&
+                 global_timer_ns() - t0 < 1000000ull) {
+          }
+        }
+      }
+    } else if (warp == 10 || warp == 11) {
+      // ------------------------------------------------------------------ MMA issuers
+      // Per step: one combined wait (both units' K/V slots landed, P of step s-3 written), then
+      // PV(s-3) for both units and QK(s) for both units, as in tc_fwd_kernel.
+      const int X = warp - 10;
+      volatile int* item_slot = item_slots + 2 * X;
+      const uint32_t tcol = tmem + 256 * X;
+      const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV + X * kStages * kStageBytes), 16, 1024);
+      uint32_t qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
+      bool solo = false;                  // the current item (PVs never cross an item)
+      bool ok = true;
+      // PV of step s (both units) from V stage s % kPairVStages; the caller has waited for P(s),
+      // V(s) and, on an item's first PV, for the epilogue to have read the previous item's O.
+      auto emit_pv = [&](uint32_t s, bool first) {
+        const uint32_t sbuf = s % 3;
+        const int vs = kPairKStages + (int)(s % kPairVStages);
+        if (elect_one()) {
+          const uint64_t va = kdesc0 + (uint64_t)((vs * kStageBytes) >> 4);
+          const uint64_t vb = va + (uint64_t)(kKBytes >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_ts(tcol + 192, tcol + 64 * sbuf + 8 * kk, va + (uint64_t)((2048 * kk) >> 4), kIdescPV64,
+                        (first && kk == 0) ? 0u : 1u);
+          if (!solo) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ts(tcol + 192 + kLane16, tcol + 64 * sbuf + 8 * kk + kLane16,
+                          vb + (uint64_t)((2048 * kk) >> 4), kIdescPV64, (first && kk == 0) ? 0u : 1u);
+          }
+          mma_commit(&bars->o_done[X][s & 1]);
+          mma_commit(&bars->kv_empty[X][vs]);
+        }
+        __syncwarp();
+      };
+      auto issue_pv = [&]() -> bool {
+        const uint32_t s = pvs;
+        if (!warp_mbar_wait2(&bars->p_full[X][s % 3], (s / 3) & 1, &bars->kv_full[X][kPairKStages + s % kPairVStages],
+                             (s / kPairVStages) & 1, true, abort))
+          return false;
+        const bool first = (s == item_first);
+        if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
+        tc_fence_after();
+        emit_pv(s, first);
+        ++pvs;
+        return true;
+      };
+      for (uint32_t k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
+        const int item = item_slot[slot];
+        __syncwarp();
+        if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
+        __syncwarp();
+        if (item < 0) break;
+        const PItem w = decode_pair(a, rowptr, item);
+        const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
+        int last_used = -1;
+        if (count_steps(entries, w.e0, w.n, fa, last_used) == 0) continue;
+        const int qs = qk % kQSlots;
+        if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
+        ++qk;
+        const uint32_t qaddr = smem_u32(smem + kOffQ + (kQSlots * X + qs) * kQBytes);
+        const uint64_t qda = sw128_desc(qaddr, 16, 1024), qdb = sw128_desc(qaddr + kQBytes / 2, 16, 1024);
+        item_first = steps;
+        solo = w.solo;
+        int32_t held = 0;
+        int base = -32;
+        for (int i = 0; i < w.n && ok; ++i) {
+          const int32_t e = entry_at(entries, w, i, held, base);
+          if (!(e & fa)) continue;
+          const int ks = steps % kPairKStages;
+          while (ok && pvs + kPvLag < steps) ok = issue_pv();
+          if (!ok) break;
+          const bool pv_now = pvs + kPvLag == steps;
+          const uint32_t ps = pvs;
+          const bool pv_first = pv_now && ps == item_first;
+          if (pv_first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) { ok = false; break; }
+          if (!warp_mbar_wait2(&bars->kv_full[X][ks], (steps / kPairKStages) & 1, &bars->p_full[X][ps % 3],
+                               (ps / 3) & 1, pv_now, abort) ||
+              (pv_now && !warp_mbar_wait(&bars->kv_full[X][kPairKStages + ps % kPairVStages],
+                                         (ps / kPairVStages) & 1, abort))) { ok = false; break; }
+          const uint32_t sb = steps % 3;
+          tc_fence_after();
+          if (pv_now) emit_pv(ps, pv_first);
+          if (elect_one()) {
+            const uint64_t ka = kdesc0 + (uint64_t)((ks * kStageBytes) >> 4);
+            const uint64_t kb = ka + (uint64_t)(kKBytes >> 4);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ss(tcol + 64 * sb, qda + 2 * kk, ka + 2 * kk, kIdescQK64, kk > 0 ? 1u : 0u);
+            if (!solo) {
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_bf16_ss(tcol + 64 * sb + kLane16, qdb + 2 * kk, kb + 2 * kk, kIdescQK64, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&bars->s_full[X][sb]);
+            mma_commit(&bars->kv_empty[X][ks]);
+            if (i == last_used) mma_commit(&bars->q_empty[X][qs]);
+          }
+          __syncwarp();
+          if (pv_now) ++pvs;
+          ++steps;
+        }
+        if (!ok) break;
+        while (ok && pvs < steps) ok = issue_pv();
+        if (!ok) break;
+        if (steps > item_first) ++titems;
+      }
+      if (!ok && lane == 0) fail(abort, 3);
+      if (elect_one()) mma_commit(&bars->drain);
+      __syncwarp();
+      if (lane == 0) {
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&bars->drain, 0) && global_timer_ns() - t0 < kWaitLimitNs) {
+        }
+      }
+      __syncwarp();
+    } else {
+      // ------------------------------------------------------------------ softmax + epilogue
+      const int X = warp >> 2;                 // tile worker
+      const bool upper = lane >= 16;           // partner unit's lanes
+      const int r64 = 16 * (warp & 3) + (lane & 15);   // query row within chunk j
+      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+      const uint32_t tcol = tmem + 256 * X;
+      volatile int* item_slot = item_slots + 2 * X;
+      uint64_t* s_full = bars->s_full[X];
+      uint64_t* p_full = bars->p_full[X];
+      uint64_t* o_done = bars->o_done[X];
+      uint64_t* o_free = &bars->o_free[X];
+      uint32_t it = 0, sb_c = 0, ph_c = 0;
+      bool s_ready = false;
+      bool ok = true;
+      for (uint32_t k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
+        const int item = item_slot[slot];
+        mbar_arrive(&bars->item_empty[X][slot]);
+        if (item < 0) break;
+        const PItem w = decode_pair(a, rowptr, item);
+        const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
+        const int32_t fd = (w.j & 1) ? kFlagDiag1 : kFlagDiag0;
+        const bool live = !(w.solo && upper);
+        float m = -INFINITY, l = 0.f;
+        int nsteps = 0;
+        for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
+          const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
+          uint32_t own = __ballot_sync(0xffffffffu, (eb & fa) != 0);
+          while (own) {
+            const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
+            own &= own - 1;
+            ++nsteps;
+            const uint32_t sb = sb_c;
+            if (!s_ready && !warp_mbar_wait(&s_full[sb], ph_c, abort)) { ok = false; break; }
+            tc_fence_after();
+            uint32_t sr[64];
+            XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
+            XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
+            const bool next_done = mbar_test_wait(&s_full[sb_c == 2 ? 0 : sb_c + 1], sb_c == 2 ? ph_c ^ 1u : ph_c);
+            XSAKE_TMEM_WAIT_LD32(sr);
+            XSAKE_TMEM_WAIT_LD32((sr + 32));
+            s_ready = __all_sync(0xffffffffu, next_done);
+            uint32_t pk[32];
+            float* x = reinterpret_cast<float*>(sr);   // raw scores
+            // Keys past the token-level causal cut on the diagonal chunk, and every key of a
+            // lane whose unit is absent (a lone unit), are masked.
+            const int lim = !live ? -1 : ((e & fd) ? r64 : 63);
+            if (__any_sync(0xffffffffu, lim < 63)) {
+#pragma unroll
+              for (int j = 0; j < 64; ++j)
+                if (j > lim) x[j] = -INFINITY;
+            }
+            float t1[22];
+#pragma unroll
+            for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+            t1[21] = x[63];
+            float t2[8];
+#pragma unroll
+            for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
+            t2[7] = t1[21];
+            const float mraw =
+                fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
+            const float mx = mraw * p.scale_log2;
+            const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
+            if (m == -INFINITY) m = mx;
+            if (__any_sync(0xffffffffu, need)) {
+              if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
+              tc_fence_after();
+              const float alpha = need ? ex2(m - mx) : 1.0f;
+              uint32_t orow[32];
+#pragma unroll
+              for (int hcol = 0; hcol < 2; ++hcol) {
+                XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
+                XSAKE_TMEM_WAIT_LD32(orow);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
+                XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
+              }
+              tmem_wait_st();
+              if (need) {
+                l *= alpha;
+                m = mx;
+              }
+            }
+            const float msub = (m == -INFINITY) ? 0.f : m;
+            const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
+            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float x0, x1, p0, p1;
+              upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
+              if ((j & 7) < 2) {
+                exp2_poly2(x0, x1, p0, p1);
+              } else {
+                p0 = ex2(x0);
+                p1 = ex2(x1);
+              }
+              acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
+              __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+              pk[j] = *reinterpret_cast<uint32_t*>(&pb);
+            }
+            float s0, s1;
+            upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
+            l += s0 + s1;
+            XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&p_full[sb]);
+            ++it;
+            if (++sb_c == 3) {
+              sb_c = 0;
+              ph_c ^= 1;
+            }
+          }
+        }
+        if (!ok) break;
+        // ---------------------------------------------------------------- epilogue
+        const int bb = upper ? w.b1 : w.b0, hh = upper ? w.h1 : w.h0;
+        const int tok = 64 * w.j + r64;
+        const bool valid = live && tok < a.S;
+        const bool empty = valid && !(l > 0.f);
+        uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + bb * a.os[0] +
+                                                 hh * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
+        if (nsteps > 0) {
+          // The same two-phase wait for the last PVs as in tc_fwd_kernel.
+          if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
+          if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
+          tc_fence_after();
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+          for (int hcol = 0; hcol < 2; ++hcol) {
+            uint32_t orow[32];
+            XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
+            XSAKE_TMEM_WAIT_LD32(orow);
+            if (valid && !empty) {
+#pragma unroll
+              for (int cc = 0; cc < 4; ++cc) {
+                uint32_t wv[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  __nv_bfloat162 pb = __floats2bfloat162_rn(__uint_as_float(orow[8 * cc + 2 * q]) * inv,
+                                                            __uint_as_float(orow[8 * cc + 2 * q + 1]) * inv);
+                  wv[q] = *reinterpret_cast<uint32_t*>(&pb);
+                }
+                orow_g[4 * hcol + cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+              }
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(o_free);
+        }
+        const bool empty_lo = __any_sync(0xffffffffu, empty && !upper);
+        const bool empty_hi = __any_sync(0xffffffffu, empty && upper);
+        if (empty_lo || empty_hi) {
+          // Rows with no live score attend uniformly (the reference's finfo.min fill).
+          float2 mean0 = make_float2(0.f, 0.f), mean1 = make_float2(0.f, 0.f);
+          if (empty_lo) warp_mean_v(a, w.b0, w.h0, mean0);
+          if (empty_hi) warp_mean_v(a, w.b1, w.h1, mean1);
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc) {
+            uint32_t wv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int src = 4 * cc + q;
+              const float x0 = __shfl_sync(0xffffffffu, mean0.x, src), y0 = __shfl_sync(0xffffffffu, mean0.y, src);
+              const float x1 = __shfl_sync(0xffffffffu, mean1.x, src), y1 = __shfl_sync(0xffffffffu, mean1.y, src);
+              __nv_bfloat162 pb = __floats2bfloat162_rn(upper ? x1 : x0, upper ? y1 : y0);
+              wv[q] = *reinterpret_cast<uint32_t*>(&pb);
+            }
+            if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          }
+        }
+        if (valid) a.lse[(int64_t)(bb * a.H + hh) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
+      }
+      if (!ok) fail(abort, 4);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 constexpr int kMaxDev = 64;
 std::once_flag g_attr_once[kMaxDev];
 cudaError_t g_attr_err[kMaxDev];
+std::once_flag g_pair_attr_once[kMaxDev];
+cudaError_t g_pair_attr_err[kMaxDev];
 
 }  // namespace
 
@@ -661,22 +1178,37 @@ int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
                 di.minor);
   XSAKE_REQUIRE(ws != nullptr && ws_bytes >= 256 && ((uintptr_t)ws & 15) == 0, XSAKE_EINVAL,
                 "the tensor-core forward needs a 256-byte, 16-byte aligned workspace (got %zu bytes)", ws_bytes);
+  // Units that share a mask are paired (tc_fwd_pair_kernel) whenever there are two of them;
+  // a mask per unit leaves only the query-chunk pairing of tc_fwd_kernel.
+  const bool paired = pair_units(a.L, a.B, a.H) >= 2;
   CUtensorMap mq, mk, mv;
-  if ((st = tc_make_map(&mq, a.q, a.qs, a.B, a.H, a.S, 128))) return st;
+  if ((st = tc_make_map(&mq, a.q, a.qs, a.B, a.H, a.S, paired ? 64 : 128))) return st;
   if ((st = tc_make_map(&mk, a.k, a.ks, a.B, a.H, a.S, 64))) return st;
   if ((st = tc_make_map(&mv, a.v, a.vs, a.B, a.H, a.S, 64))) return st;
   int dev = 0;
   XSAKE_CUDA_TRY(cudaGetDevice(&dev));
   XSAKE_REQUIRE(dev < kMaxDev, XSAKE_EUNSUPPORTED, "device ordinal %d", dev);
+  TcParams p;
+  p.a = a;
+  p.scale_log2 = a.scale * kLog2e;
+  p.counter = reinterpret_cast<int*>(ws);
+  if (paired) {
+    std::call_once(g_pair_attr_once[dev], [dev] {
+      g_pair_attr_err[dev] =
+          cudaFuncSetAttribute(tc_fwd_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    });
+    XSAKE_REQUIRE(g_pair_attr_err[dev] == cudaSuccess, XSAKE_ECUDA, "cudaFuncSetAttribute: %s",
+                  cudaGetErrorString(g_pair_attr_err[dev]));
+    XSAKE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(int), s));
+    const int grid = std::max(1, std::min((pair_items(a.L, a.B, a.H) + 1) / 2, di.sm_count));
+    tc_fwd_pair_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
+    return check_launch("tc_fwd_pair_kernel");
+  }
   std::call_once(g_attr_once[dev], [dev] {
     g_attr_err[dev] = cudaFuncSetAttribute(tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   });
   XSAKE_REQUIRE(g_attr_err[dev] == cudaSuccess, XSAKE_ECUDA, "cudaFuncSetAttribute: %s",
                 cudaGetErrorString(g_attr_err[dev]));
-  TcParams p;
-  p.a = a;
-  p.scale_log2 = a.scale * kLog2e;
-  p.counter = reinterpret_cast<int*>(ws);
   XSAKE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(int), s));
   const int grid = std::max(1, std::min((a.L.nitems + 1) / 2, di.sm_count));
   tc_fwd_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
