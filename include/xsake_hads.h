@@ -142,6 +142,23 @@ XSAKE_API int xsake_layernorm_bwd(int32_t x_dtype, int64_t rows, int64_t d, cons
                         const void* dy_dev, void* dx_dev, float* dgamma_dev, float* dbeta_dev,
                         void* workspace_dev, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ cross entropy
+ * cross_entropy_loss (model/transformer.py:177-203) of the config-4 training step, over
+ * `rows` rows of logits (dtype XSAKE_F32 / XSAKE_BF16; the vocabulary is the last axis, ld
+ * elements between rows, ld >= vocab).  targets_dev int64 [rows]; a target equal to
+ * ignore_index contributes nothing (the reference's `valid` mask); other targets are clamped
+ * to [0, vocab).  Forward: lse_dev[r] = log(sum exp logits[r]) and nll_dev[r] = lse - logit of
+ * the target (0 when ignored), fp32 arithmetic; the caller sums nll and divides by the number
+ * of valid rows.  Backward: grad_dev (same dtype and ld as the logits) receives
+ * *coef_dev * (softmax - onehot(target)) in the vocab columns, 0 in columns [vocab, ld) and in
+ * ignored rows; coef_dev is a device fp32 scalar (d loss / d sum of nll). */
+XSAKE_API int xsake_xent_fwd(int32_t dtype, int64_t rows, int64_t vocab, int64_t ld, const void* logits_dev,
+                   const int64_t* targets_dev, int64_t ignore_index, float* lse_dev, float* nll_dev,
+                   void* stream);
+XSAKE_API int xsake_xent_bwd(int32_t dtype, int64_t rows, int64_t vocab, int64_t ld, const void* logits_dev,
+                   const int64_t* targets_dev, int64_t ignore_index, const float* lse_dev,
+                   const float* coef_dev, void* grad_dev, void* stream);
+
 /* ------------------------------------------------------------------ HADS calibration
  * compute_attention_entropy (kernels/hads/hads_pattern.py:36-50): p fp32
  * [B, H, Sq, Sk] contiguous; head_sums_dev[h] (fp64) receives sum over (b, q) of

@@ -43,6 +43,40 @@ def _torch_forward(model, ids):
     return F.linear(x, model.tok.weight)
 
 
+def _torch_xent(logits, labels, ignore_index=-1):
+    """cross_entropy_loss of model/transformer.py:177-203 with plain torch ops (fp32)."""
+    vocab = logits.shape[-1]
+    fl = logits[:, :-1].reshape(-1, vocab).float()
+    lb = labels[:, 1:].reshape(-1)
+    valid = lb != ignore_index
+    nll = F.cross_entropy(fl, lb.clamp(0, vocab - 1), reduction="none")
+    return (nll * valid).sum() / valid.sum().clamp(min=1)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("vocab,ld", [(97, 128), (50257, 50304), (33, 33)])
+def test_fused_cross_entropy_matches_torch(dtype, vocab, ld):
+    # Logits as a [..., :vocab] view of a padded buffer (the model's layout; 16-byte vector
+    # path) and a contiguous buffer with an odd row length (scalar path), with ignored targets.
+    from xsake_b200.model import cross_entropy_loss
+    torch.manual_seed(3)
+    B, S = 2, (96 if vocab > 1000 else 300)
+    buf = (3 * torch.randn(B, S, ld, device="cuda")).to(dtype)
+    labels = torch.randint(0, vocab, (B, S), device="cuda")
+    labels[0, 5] = -1
+    labels[1, 7] = -1
+    src = buf.clone().requires_grad_(True)
+    loss = cross_entropy_loss(src[..., :vocab], labels)
+    loss.backward()
+    ref_src = buf.float().clone().requires_grad_(True)
+    ref = _torch_xent(ref_src[..., :vocab], labels)
+    ref.backward()
+    assert abs(loss.item() - ref.item()) <= 1e-5 * abs(ref.item()), (loss.item(), ref.item())
+    g, rg = src.grad.float(), ref_src.grad
+    tol = 1e-6 if dtype == torch.float32 else 1e-2 * rg.abs().max().item()
+    assert (g - rg).abs().max().item() <= tol, (g - rg).abs().max().item()
+
+
 def test_model_loss_and_grads_match_torch_composition():
     from xsake_b200.model import XSAKETransformer, cross_entropy_loss
     torch.manual_seed(0)
@@ -55,7 +89,7 @@ def test_model_loss_and_grads_match_torch_composition():
     loss.backward()
     got = {n: p.grad.detach().clone() for n, p in model.named_parameters()}
     model.zero_grad(set_to_none=True)
-    ref_loss = cross_entropy_loss(_torch_forward(model, ids.clamp(min=0)), ids)
+    ref_loss = _torch_xent(_torch_forward(model, ids.clamp(min=0)), ids)
     ref_loss.backward()
     assert abs(loss.item() - ref_loss.item()) <= 1e-4 * abs(ref_loss.item())
     gmax = max(p.grad.abs().max().item() for p in model.parameters())

@@ -100,13 +100,16 @@ def test_layernorm_config1_bf16():
 
 
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
-def test_layernorm_backward(dtype):
+@pytest.mark.parametrize("rows,d", [(300, 768), (1000, 64), (257, 1024), (300, 100), (129, 1536)])
+def test_layernorm_backward(dtype, rows, d):
+    # d = 64, 768, 1024: register-resident kernel (1024 fp32 and 1536 are too wide for it, 100
+    # is not a whole number of 16-byte vectors): the row-loop kernel.
     from xsake_b200.fused_layernorm import layernorm_backward, layernorm_forward
     rng = np.random.default_rng(5)
-    x = rng.standard_normal((300, 768)).astype(np.float32)
-    g = (1 + 0.1 * rng.standard_normal(768)).astype(np.float32)
-    b = (0.1 * rng.standard_normal(768)).astype(np.float32)
-    dy = rng.standard_normal((300, 768)).astype(np.float32)
+    x = rng.standard_normal((rows, d)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    dy = rng.standard_normal((rows, d)).astype(np.float32)
     tdt = torch.float32 if dtype == "f32" else torch.bfloat16
     if dtype == "bf16":
         x, dy = oi.to_bf16(x).astype(np.float32), oi.to_bf16(dy).astype(np.float32)

@@ -57,6 +57,8 @@ _SIGS = {
     "xsake_softmax_bwd": (C.c_int, [_I32, _I64, _I64, _VP, _VP, _VP, _VP]),
     "xsake_layernorm_fwd": (C.c_int, [_I32, _I64, _I64, _VP, _VP, _VP, _F, _VP, _VP, _VP, _VP]),
     "xsake_layernorm_bwd_workspace_size": (C.c_int, [_I64, _I64, C.POINTER(_SZ)]),
+    "xsake_xent_fwd": (C.c_int, [_I32, _I64, _I64, _I64, _VP, _VP, _I64, _VP, _VP, _VP]),
+    "xsake_xent_bwd": (C.c_int, [_I32, _I64, _I64, _I64, _VP, _VP, _I64, _VP, _VP, _VP, _VP]),
     "xsake_layernorm_bwd": (C.c_int, [_I32, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP,
                                       _VP, _SZ, _VP]),
     "xsake_entropy_workspace_size": (C.c_int, [_I64, _I64, _I64, C.POINTER(_SZ)]),

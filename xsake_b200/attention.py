@@ -24,6 +24,22 @@ from . import sparsity_mask as sm
 from .sparse_attention import attention_probabilities, sparse_attention_autograd
 
 
+# Masks built from layer parameters alone (the uncalibrated HADS profile, the fixed patterns) are
+# deterministic, so they are built once per parameter set and shared, read-only, by every layer
+# and call.  The reference builds them on the host at trace time, i.e. once per compiled step;
+# rebuilding the dummy profile on every call cost ~10 ms of host time per layer at S=4096.
+_MASKS: dict = {}
+
+
+def _cached_mask(key, build):
+    m = _MASKS.get(key)
+    if m is None:
+        m = np.ascontiguousarray(build(), dtype=bool)
+        m.setflags(write=False)
+        _MASKS[key] = m
+    return m
+
+
 class XSAKEAttention(nn.Module):
     """Drop-in for model/attention.py's XSAKEAttention.
 
@@ -72,10 +88,13 @@ class XSAKEAttention(nn.Module):
         if self.hads_profile is not None:
             return np.asarray(self.hads_profile.block_masks, bool), bs
         if self.sparsity_type == "hads":
-            prof = hp.dummy_hads_profile(self.n_heads, seq, bs, self.min_sparsity, self.max_sparsity,
-                                         self.window_size, causal=True)
-            return prof.block_masks, bs
-        return sm.make_block_mask(seq, bs, self.sparsity_type, sparsity_ratio=0.5, causal=True), bs
+            key = ("hads", self.n_heads, seq, bs, self.min_sparsity, self.max_sparsity, self.window_size)
+            return _cached_mask(key, lambda: hp.dummy_hads_profile(
+                self.n_heads, seq, bs, self.min_sparsity, self.max_sparsity, self.window_size,
+                causal=True).block_masks), bs
+        key = (self.sparsity_type, seq, bs)
+        return _cached_mask(key, lambda: sm.make_block_mask(seq, bs, self.sparsity_type, sparsity_ratio=0.5,
+                                                            causal=True)), bs
 
     def forward(self, x: torch.Tensor, mask: Optional[torch.Tensor] = None, training: Optional[bool] = None,
                 collect_attn: bool = False):

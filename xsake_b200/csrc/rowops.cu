@@ -347,6 +347,110 @@ __global__ void __launch_bounds__(256) layernorm_bwd_rows(const T* __restrict__ 
   for (int64_t c = threadIdx.x; c < 2 * d; c += blockDim.x) partial[(int64_t)blockIdx.x * 2 * d + c] = sacc[c];
 }
 
+// Register-resident backward for rows of 16-byte vectors: each warp owns whole rows (contiguous
+// per-CTA ranges, as above), loads x and dy once with 16-byte loads, writes dx from registers and
+// keeps its lanes' column partials (sum dy*xhat, sum dy) in registers across its rows; the CTA's
+// warps are then summed in a fixed order, so the result stays deterministic.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(256) layernorm_bwd_reg(const T* __restrict__ x, const float* __restrict__ gamma,
+                                                         const float* __restrict__ mean_in,
+                                                         const float* __restrict__ rstd_in, const T* __restrict__ dy,
+                                                         T* __restrict__ dx, float* __restrict__ partial,
+                                                         int64_t rows, int64_t d) {
+  constexpr int N = Vec<T>::N;
+  extern __shared__ float4 sm4[];
+  float* sg = reinterpret_cast<float*>(sm4);   // gamma [d]
+  float* wp = sg + d;                          // per-warp column partials [warps][2][d]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t nvec = d / N;
+  for (int64_t c = threadIdx.x; c < d / 4; c += blockDim.x) sm4[c] = reinterpret_cast<const float4*>(gamma)[c];
+  __syncthreads();
+  const float4* sg4 = sm4;
+  const float inv_d = 1.f / (float)d;
+  const int64_t per = (rows + gridDim.x - 1) / gridDim.x;
+  const int64_t r0 = (int64_t)blockIdx.x * per, r1 = min(rows, r0 + per);
+  float cg[VPL][N], cb[VPL][N];
+#pragma unroll
+  for (int k = 0; k < VPL; ++k)
+#pragma unroll
+    for (int i = 0; i < N; ++i) cg[k][i] = cb[k][i] = 0.f;
+  for (int64_t row = r0 + warp; row < r1; row += kWarpsPerBlock) {
+    const float mean = mean_in[row], rstd = rstd_in[row];
+    float xh[VPL][N], g[VPL][N];
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+        Vec<T>::load(x + row * d + vi * N, xh[k]);
+        Vec<T>::load(dy + row * d + vi * N, g[k]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) xh[k][i] = g[k][i] = 0.f;
+      }
+    }
+    float a1 = 0.f, a2 = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+#pragma unroll
+        for (int j = 0; j < N / 4; ++j) {
+          const float4 gm = sg4[vi * (N / 4) + j];
+          const float gg[4] = {gm.x, gm.y, gm.z, gm.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int i = 4 * j + q;
+            xh[k][i] = (xh[k][i] - mean) * rstd;
+            const float gd = gg[q] * g[k][i];
+            a1 += gd;
+            a2 = fmaf(gd, xh[k][i], a2);
+            cg[k][i] = fmaf(g[k][i], xh[k][i], cg[k][i]);
+            cb[k][i] += g[k][i];
+          }
+        }
+      }
+    }
+    a1 = warp_sum(a1) * inv_d;
+    a2 = warp_sum(a2) * inv_d;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int64_t vi = lane + 32 * k;
+      if (vi < nvec) {
+        float o[N];
+#pragma unroll
+        for (int j = 0; j < N / 4; ++j) {
+          const float4 gm = sg4[vi * (N / 4) + j];
+          const float gg[4] = {gm.x, gm.y, gm.z, gm.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int i = 4 * j + q;
+            o[i] = rstd * (gg[q] * g[k][i] - a1 - xh[k][i] * a2);
+          }
+        }
+        Vec<T>::store(dx + row * d + vi * N, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < VPL; ++k) {
+    const int64_t vi = lane + 32 * k;
+    if (vi < nvec) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        wp[(int64_t)(2 * warp) * d + vi * N + i] = cg[k][i];
+        wp[(int64_t)(2 * warp + 1) * d + vi * N + i] = cb[k][i];
+      }
+    }
+  }
+  __syncthreads();
+  for (int64_t c = threadIdx.x; c < 2 * d; c += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarpsPerBlock; ++w) acc += wp[(int64_t)w * 2 * d + c];
+    partial[(int64_t)blockIdx.x * 2 * d + c] = acc;
+  }
+}
+
 __global__ void ln_bwd_reduce(const float* __restrict__ partial, int nblocks, int64_t d, float* __restrict__ dgamma,
                               float* __restrict__ dbeta) {
   const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -354,6 +458,113 @@ __global__ void ln_bwd_reduce(const float* __restrict__ partial, int nblocks, in
   float acc = 0.f;
   for (int b = 0; b < nblocks; ++b) acc += partial[(int64_t)b * 2 * d + c];
   if (c < d) dgamma[c] = acc; else dbeta[c - d] = acc;
+}
+
+// ------------------------------------------------------------------------------ cross entropy
+// cross_entropy_loss of model/transformer.py:177-203 over rows of logits (the vocabulary in the
+// last axis, `ld` elements between rows, ld >= vocab).  One warp per row.  Forward: online max /
+// sum of exp in fp32 from the logits' own dtype, lse = max + log(sum), nll = lse - logit[target]
+// (0 for a target equal to ignore_index).  Backward: grad = coef * (softmax - onehot(target)) for
+// the vocab columns and 0 for columns [vocab, ld) and for ignored rows, written over the whole
+// row so the gradient buffer needs no fill.  coef (a device scalar) is d(loss)/d(sum of nll).
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) xent_fwd_kernel(const T* __restrict__ logits, int64_t rows, int64_t vocab,
+                                                       int64_t ld, const int64_t* __restrict__ targets,
+                                                       int64_t ignore_index, float* __restrict__ lse_out,
+                                                       float* __restrict__ nll_out) {
+  constexpr int N = Vec<T>::N;
+  constexpr float kL2e = 1.4426950408889634f;
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    const T* r = logits + row * ld;
+    float m = -INFINITY, sum = 0.f;
+    auto add = [&](const float* v, int n) {
+      float mv = v[0];
+      for (int i = 1; i < n; ++i) mv = fmaxf(mv, v[i]);
+      if (mv > m) {
+        sum = m == -INFINITY ? 0.f : sum * exp2f((m - mv) * kL2e);
+        m = mv;
+      }
+      if (m != -INFINITY)
+        for (int i = 0; i < n; ++i) sum += exp2f((v[i] - m) * kL2e);
+    };
+    int64_t c0 = 0;
+    if (VEC) {
+      const int64_t nv = vocab / N;
+      for (int64_t vi = lane; vi < nv; vi += 32) {
+        float v[N];
+        Vec<T>::load(r + vi * N, v);
+        add(v, N);
+      }
+      c0 = nv * N;
+    }
+    for (int64_t c = c0 + lane; c < vocab; c += 32) {
+      const float v = DT<T>::to_f(r[c]);
+      add(&v, 1);
+    }
+    // Combine the lanes' (max, sum) pairs.
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float mo = __shfl_xor_sync(0xffffffffu, m, off), so = __shfl_xor_sync(0xffffffffu, sum, off);
+      const float mn = fmaxf(m, mo);
+      sum = (m == -INFINITY ? 0.f : sum * exp2f((m - mn) * kL2e)) +
+            (mo == -INFINITY ? 0.f : so * exp2f((mo - mn) * kL2e));
+      m = mn;
+    }
+    if (lane == 0) {
+      const float lse = m + logf(sum);
+      const int64_t t = targets[row];
+      const bool valid = t != ignore_index;
+      const int64_t tc = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+      lse_out[row] = lse;
+      nll_out[row] = valid ? lse - DT<T>::to_f(r[tc]) : 0.f;
+    }
+  }
+}
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) xent_bwd_kernel(const T* __restrict__ logits, int64_t rows, int64_t vocab,
+                                                       int64_t ld, const int64_t* __restrict__ targets,
+                                                       int64_t ignore_index, const float* __restrict__ lse_in,
+                                                       const float* __restrict__ coef, T* __restrict__ grad) {
+  constexpr int N = Vec<T>::N;
+  constexpr float kL2e = 1.4426950408889634f;
+  const int lane = threadIdx.x & 31;
+  const float cf = *coef;
+  for (int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5); row < rows;
+       row += (int64_t)gridDim.x * kWarpsPerBlock) {
+    const T* r = logits + row * ld;
+    T* gr = grad + row * ld;
+    const int64_t t = targets[row];
+    const bool valid = t != ignore_index;
+    const int64_t tc = t < 0 ? 0 : (t >= vocab ? vocab - 1 : t);
+    const float nl = -lse_in[row] * kL2e;
+    const float c = valid ? cf : 0.f;
+    auto g_of = [&](int64_t col, float x) {
+      if (col >= vocab) return 0.f;
+      return c * (exp2f(fmaf(x, kL2e, nl)) - (col == tc ? 1.f : 0.f));
+    };
+    int64_t c0 = 0;
+    if (VEC) {
+      const int64_t nv = ld / N;   // whole rows of vectors: ld % N == 0
+      for (int64_t vi = lane; vi < nv; vi += 32) {
+        float v[N], o[N];
+        if ((vi + 1) * N <= vocab) {
+          Vec<T>::load(r + vi * N, v);
+        } else {
+#pragma unroll
+          for (int i = 0; i < N; ++i) v[i] = vi * N + i < vocab ? DT<T>::to_f(r[vi * N + i]) : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) o[i] = g_of(vi * N + i, v[i]);
+        Vec<T>::store(gr + vi * N, o);
+      }
+      c0 = nv * N;
+    }
+    for (int64_t col = c0 + lane; col < ld; col += 32)
+      gr[col] = DT<T>::from_f(g_of(col, col < vocab ? DT<T>::to_f(r[col]) : 0.f));
+  }
 }
 
 int grid_for_rows(int64_t rows, int sm_count, int ctas_per_sm = 32) {
@@ -514,6 +725,39 @@ extern "C" int xsake_layernorm_bwd(int32_t x_dtype, int64_t rows, int64_t d, con
   cudaStream_t s = as_stream(stream);
   const size_t smem = 2 * d * sizeof(float);
   float* partial = reinterpret_cast<float*>(workspace_dev);
+  // Rows of whole 16-byte vectors, up to 6 (fp32) or 4 (bf16) vectors a lane (d <= 768 fp32,
+  // d <= 1024 bf16; wider rows would spill): the register-resident kernel.
+  const int nvec_lane = x_dtype == XSAKE_F32 ? (int)((d / 4 + 31) / 32) : (int)((d / 8 + 31) / 32);
+  const bool vec_ok = d % 8 == 0 && ((uintptr_t)x_dev & 15) == 0 && ((uintptr_t)dy_dev & 15) == 0 &&
+                      ((uintptr_t)dx_dev & 15) == 0 && ((uintptr_t)gamma_dev & 15) == 0 &&
+                      nvec_lane <= (x_dtype == XSAKE_F32 ? 6 : 4);
+  const size_t smem_reg = (size_t)(1 + 2 * kWarpsPerBlock) * d * sizeof(float);
+  if (vec_ok && smem_reg <= 200 * 1024) {
+    auto launch = [&](auto kern, auto xp, auto dyp, auto dxp) -> int {
+      XSAKE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_reg));
+      kern<<<nb, 256, smem_reg, s>>>(xp, gamma_dev, mean_dev, rstd_dev, dyp, dxp, partial, rows, d);
+      return check_launch("layernorm_bwd_reg");
+    };
+    if (x_dtype == XSAKE_F32) {
+      const float* xp = (const float*)x_dev;
+      const float* dyp = (const float*)dy_dev;
+      float* dxp = (float*)dx_dev;
+      if (nvec_lane <= 2) st = launch(layernorm_bwd_reg<float, 2>, xp, dyp, dxp);
+      else if (nvec_lane <= 4) st = launch(layernorm_bwd_reg<float, 4>, xp, dyp, dxp);
+      else st = launch(layernorm_bwd_reg<float, 6>, xp, dyp, dxp);
+    } else {
+      const __nv_bfloat16* xp = (const __nv_bfloat16*)x_dev;
+      const __nv_bfloat16* dyp = (const __nv_bfloat16*)dy_dev;
+      __nv_bfloat16* dxp = (__nv_bfloat16*)dx_dev;
+      if (nvec_lane <= 1) st = launch(layernorm_bwd_reg<__nv_bfloat16, 1>, xp, dyp, dxp);
+      else if (nvec_lane <= 2) st = launch(layernorm_bwd_reg<__nv_bfloat16, 2>, xp, dyp, dxp);
+      else if (nvec_lane <= 3) st = launch(layernorm_bwd_reg<__nv_bfloat16, 3>, xp, dyp, dxp);
+      else st = launch(layernorm_bwd_reg<__nv_bfloat16, 4>, xp, dyp, dxp);
+    }
+    if (st) return st;
+    ln_bwd_reduce<<<(int)((2 * d + 255) / 256), 256, 0, s>>>(partial, nb, d, dgamma_dev, dbeta_dev);
+    return check_launch("ln_bwd_reduce");
+  }
   if (x_dtype == XSAKE_F32) {
     if (smem > 48 * 1024)
       XSAKE_CUDA_TRY(cudaFuncSetAttribute(layernorm_bwd_rows<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -530,4 +774,58 @@ extern "C" int xsake_layernorm_bwd(int32_t x_dtype, int64_t rows, int64_t d, con
   if ((st = check_launch("layernorm_bwd_rows"))) return st;
   ln_bwd_reduce<<<(int)((2 * d + 255) / 256), 256, 0, s>>>(partial, nb, d, dgamma_dev, dbeta_dev);
   return check_launch("ln_bwd_reduce");
+}
+
+extern "C" int xsake_xent_fwd(int32_t dtype, int64_t rows, int64_t vocab, int64_t ld, const void* logits_dev,
+                              const int64_t* targets_dev, int64_t ignore_index, float* lse_dev, float* nll_dev,
+                              void* stream) {
+  clear_error();
+  int st = check_dtype(dtype);
+  if (st) return st;
+  XSAKE_REQUIRE(rows >= 0 && vocab > 0 && ld >= vocab, XSAKE_EINVAL, "need rows >= 0, vocab > 0, ld >= vocab");
+  if (rows == 0) return XSAKE_OK;
+  XSAKE_REQUIRE(logits_dev && targets_dev && lse_dev && nll_dev, XSAKE_EINVAL, "NULL pointer");
+  DeviceInfo di;
+  if ((st = device_info(&di))) return st;
+  cudaStream_t s = as_stream(stream);
+  const int grid = grid_for_rows(rows, di.sm_count, 8);
+  const bool vec = ld % 8 == 0 && ((uintptr_t)logits_dev & 15) == 0;
+  if (dtype == XSAKE_F32) {
+    const float* x = (const float*)logits_dev;
+    if (vec) xent_fwd_kernel<float, true><<<grid, 256, 0, s>>>(x, rows, vocab, ld, targets_dev, ignore_index, lse_dev, nll_dev);
+    else xent_fwd_kernel<float, false><<<grid, 256, 0, s>>>(x, rows, vocab, ld, targets_dev, ignore_index, lse_dev, nll_dev);
+  } else {
+    const __nv_bfloat16* x = (const __nv_bfloat16*)logits_dev;
+    if (vec) xent_fwd_kernel<__nv_bfloat16, true><<<grid, 256, 0, s>>>(x, rows, vocab, ld, targets_dev, ignore_index, lse_dev, nll_dev);
+    else xent_fwd_kernel<__nv_bfloat16, false><<<grid, 256, 0, s>>>(x, rows, vocab, ld, targets_dev, ignore_index, lse_dev, nll_dev);
+  }
+  return check_launch("xent_fwd_kernel");
+}
+
+extern "C" int xsake_xent_bwd(int32_t dtype, int64_t rows, int64_t vocab, int64_t ld, const void* logits_dev,
+                              const int64_t* targets_dev, int64_t ignore_index, const float* lse_dev,
+                              const float* coef_dev, void* grad_dev, void* stream) {
+  clear_error();
+  int st = check_dtype(dtype);
+  if (st) return st;
+  XSAKE_REQUIRE(rows >= 0 && vocab > 0 && ld >= vocab, XSAKE_EINVAL, "need rows >= 0, vocab > 0, ld >= vocab");
+  if (rows == 0) return XSAKE_OK;
+  XSAKE_REQUIRE(logits_dev && targets_dev && lse_dev && coef_dev && grad_dev, XSAKE_EINVAL, "NULL pointer");
+  DeviceInfo di;
+  if ((st = device_info(&di))) return st;
+  cudaStream_t s = as_stream(stream);
+  const int grid = grid_for_rows(rows, di.sm_count, 8);
+  const bool vec = ld % 8 == 0 && ((uintptr_t)logits_dev & 15) == 0 && ((uintptr_t)grad_dev & 15) == 0;
+  if (dtype == XSAKE_F32) {
+    const float* x = (const float*)logits_dev;
+    float* g = (float*)grad_dev;
+    if (vec) xent_bwd_kernel<float, true><<<grid, 256, 0, s>>>(x, rows, vocab, ld, targets_dev, ignore_index, lse_dev, coef_dev, g);
+    else xent_bwd_kernel<float, false><<<grid, 256, 0, s>>>(x, rows, vocab, ld, targets_dev, ignore_index, lse_dev, coef_dev, g);
+  } else {
+    const __nv_bfloat16* x = (const __nv_bfloat16*)logits_dev;
+    __nv_bfloat16* g = (__nv_bfloat16*)grad_dev;
+    if (vec) xent_bwd_kernel<__nv_bfloat16, true><<<grid, 256, 0, s>>>(x, rows, vocab, ld, targets_dev, ignore_index, lse_dev, coef_dev, g);
+    else xent_bwd_kernel<__nv_bfloat16, false><<<grid, 256, 0, s>>>(x, rows, vocab, ld, targets_dev, ignore_index, lse_dev, coef_dev, g);
+  }
+  return check_launch("xent_bwd_kernel");
 }

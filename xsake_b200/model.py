@@ -3,8 +3,8 @@
 PyTorch counterpart of XSAKETransformer (model/transformer.py:71-172), TransformerBlock
 (:74-104), MLP (:33-46), the LayerNorm wrapper (:51-66), TransformerEmbedding
 (model/embedding.py:63-90) and cross_entropy_loss (model/transformer.py:177-203):
-token + learned position embeddings, pre-norm blocks (fused LayerNorm in fp32 as the reference
-calls it, XSAKE attention, GELU MLP), final LayerNorm, logits tied to the token embedding.
+token + learned position embeddings, pre-norm blocks (fused LayerNorm with fp32 statistics,
+XSAKE attention, GELU MLP), final LayerNorm, logits tied to the token embedding.
 
 Attention and LayerNorm run on this library's kernels; the dense projections, embeddings and the
 optimizer are PyTorch.  The logits GEMM runs in the activation dtype with fp32 loss arithmetic
@@ -21,6 +21,8 @@ import torch
 from torch import nn
 from torch.nn import functional as F
 
+from . import _device as dev
+from . import _lib
 from . import hads_pattern as hp
 from .attention import XSAKEAttention
 from .fused_layernorm import fused_layernorm
@@ -45,7 +47,11 @@ class ModelConfig:
 
 
 class LayerNorm(nn.Module):
-    """model/transformer.py:51-66: fp32 statistics and parameters, result in x's dtype."""
+    """model/transformer.py:51-66: fp32 statistics and parameters, result in x's dtype.
+
+    The reference casts x to fp32, normalises and casts back.  The kernel reads x in its own
+    dtype and does the same fp32 arithmetic on the upcast values, so the casts (two extra passes
+    over the activations each way) are left out."""
 
     def __init__(self, d_model: int, eps: float = 1e-5, device=None):
         super().__init__()
@@ -54,7 +60,7 @@ class LayerNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x):
-        return fused_layernorm(x.float(), self.gamma.float(), self.beta.float(), eps=self.eps).to(x.dtype)
+        return fused_layernorm(x, self.gamma, self.beta, eps=self.eps)
 
 
 class MLP(nn.Module):
@@ -123,12 +129,70 @@ class XSAKETransformer(nn.Module):
             if collect_attn:
                 attn.append(w)
         x = self.ln_f(x)
-        logits = F.linear(x, self.tok.weight)    # tied to the token embedding
+        # Logits tied to the token embedding.  The GEMM runs over the vocabulary padded to a
+        # multiple of 64 rows (zeros) and the logits are the first vocab_size columns: with
+        # 50,257 columns the rows of the logits and of their gradient are not 16-byte aligned,
+        # and cuBLAS then falls back to kernels several times slower for all three GEMMs.
+        w = self.tok.weight.to(x.dtype)
+        vocab = w.shape[0]
+        pad = -vocab % 64
+        if pad:
+            w = F.pad(w, (0, 0, 0, pad))
+        logits = F.linear(x, w)[..., :vocab]
         return logits, attn
 
 
+class _CrossEntropy(torch.autograd.Function):
+    """Mean cross entropy over rows of logits [R, V] (unit column stride, any row stride) on the
+    library's fused kernels: one pass over the logits for lse and nll, one pass that writes
+    coef * (softmax - onehot) straight into the gradient; no fp32 copy of the logits is made."""
+
+    @staticmethod
+    def forward(ctx, logits, targets, ignore_index):
+        rows, vocab = logits.shape
+        lse = torch.empty(rows, dtype=torch.float32, device=logits.device)
+        nll = torch.empty_like(lse)
+        _lib.check(_lib.load().xsake_xent_fwd(
+            dev.xsake_dtype(logits), rows, vocab, logits.stride(0), logits.data_ptr(), targets.data_ptr(),
+            int(ignore_index), lse.data_ptr(), nll.data_ptr(), dev.stream_ptr()))
+        n_valid = (targets != ignore_index).sum().clamp(min=1).float()
+        ctx.save_for_backward(logits, targets, lse, n_valid)
+        ctx.ignore_index = int(ignore_index)
+        return nll.sum() / n_valid
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        logits, targets, lse, n_valid = ctx.saved_tensors
+        rows, vocab = logits.shape
+        ld = logits.stride(0)
+        coef = (grad_out.float() / n_valid).reshape(1).contiguous()
+        buf = torch.empty((rows, ld), dtype=logits.dtype, device=logits.device)
+        _lib.check(_lib.load().xsake_xent_bwd(
+            dev.xsake_dtype(logits), rows, vocab, ld, logits.data_ptr(), targets.data_ptr(), ctx.ignore_index,
+            lse.data_ptr(), coef.data_ptr(), buf.data_ptr(), dev.stream_ptr()))
+        return buf[:, :vocab], None, None
+
+
+def _fused_rows(logits: torch.Tensor):
+    """[B, S, V] logits as a [B*S, V] view with one row stride, or None."""
+    if not logits.is_cuda or logits.dtype not in (torch.float32, torch.bfloat16) or logits.dim() != 3:
+        return None
+    if logits.stride(-1) != 1 or logits.stride(0) != logits.shape[1] * logits.stride(1):
+        return None
+    return logits.view(-1, logits.shape[-1])
+
+
 def cross_entropy_loss(logits: torch.Tensor, labels: torch.Tensor, ignore_index: int = -1) -> torch.Tensor:
-    """model/transformer.py:177-203: predict token t+1 from position t, mean over valid targets."""
+    """model/transformer.py:177-203: predict token t+1 from position t, mean over valid targets.
+
+    CUDA logits go through the library's fused kernels (fp32 arithmetic on the logits' own
+    dtype): every position is a row and the last one's target is ignore_index, which is the
+    reference's [:, :-1] / [:, 1:] shift without slicing the logits."""
+    rows = _fused_rows(logits)
+    if rows is not None:
+        targets = torch.full_like(labels, ignore_index, dtype=torch.int64)
+        targets[:, :-1] = labels[:, 1:]
+        return _CrossEntropy.apply(rows, targets.reshape(-1).contiguous(), ignore_index)
     vocab = logits.shape[-1]
     flat_logits = logits[:, :-1].reshape(-1, vocab).float()
     flat_labels = labels[:, 1:].reshape(-1)
