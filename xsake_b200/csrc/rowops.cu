@@ -451,13 +451,26 @@ __global__ void __launch_bounds__(256) layernorm_bwd_reg(const T* __restrict__ x
   }
 }
 
-__global__ void ln_bwd_reduce(const float* __restrict__ partial, int nblocks, int64_t d, float* __restrict__ dgamma,
-                              float* __restrict__ dbeta) {
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= 2 * d) return;
+// Sum of the per-CTA column partials: a CTA per 32 columns, warp w adds partial rows w, w+8, ...
+// (lane = column, coalesced), then the 8 warp sums are added in order: fixed order throughout.
+__global__ void __launch_bounds__(256) ln_bwd_reduce(const float* __restrict__ partial, int nblocks, int64_t d,
+                                                     float* __restrict__ dgamma, float* __restrict__ dbeta) {
+  __shared__ float ws[kWarpsPerBlock][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
   float acc = 0.f;
-  for (int b = 0; b < nblocks; ++b) acc += partial[(int64_t)b * 2 * d + c];
-  if (c < d) dgamma[c] = acc; else dbeta[c - d] = acc;
+  if (c < 2 * d) {
+#pragma unroll 4
+    for (int b = warp; b < nblocks; b += kWarpsPerBlock) acc += partial[(int64_t)b * 2 * d + c];
+  }
+  ws[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c < 2 * d) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarpsPerBlock; ++w) t += ws[w][lane];
+    if (c < d) dgamma[c] = t; else dbeta[c - d] = t;
+  }
 }
 
 // ------------------------------------------------------------------------------ cross entropy
@@ -755,7 +768,7 @@ extern "C" int xsake_layernorm_bwd(int32_t x_dtype, int64_t rows, int64_t d, con
       else st = launch(layernorm_bwd_reg<__nv_bfloat16, 4>, xp, dyp, dxp);
     }
     if (st) return st;
-    ln_bwd_reduce<<<(int)((2 * d + 255) / 256), 256, 0, s>>>(partial, nb, d, dgamma_dev, dbeta_dev);
+    ln_bwd_reduce<<<(int)((2 * d + 31) / 32), 256, 0, s>>>(partial, nb, d, dgamma_dev, dbeta_dev);
     return check_launch("ln_bwd_reduce");
   }
   if (x_dtype == XSAKE_F32) {
@@ -772,7 +785,7 @@ extern "C" int xsake_layernorm_bwd(int32_t x_dtype, int64_t rows, int64_t d, con
         (__nv_bfloat16*)dx_dev, partial, rows, d);
   }
   if ((st = check_launch("layernorm_bwd_rows"))) return st;
-  ln_bwd_reduce<<<(int)((2 * d + 255) / 256), 256, 0, s>>>(partial, nb, d, dgamma_dev, dbeta_dev);
+  ln_bwd_reduce<<<(int)((2 * d + 31) / 32), 256, 0, s>>>(partial, nb, d, dgamma_dev, dbeta_dev);
   return check_launch("ln_bwd_reduce");
 }
 

@@ -14,6 +14,7 @@ optimizer are PyTorch.  The logits GEMM runs in the activation dtype with fp32 l
 from __future__ import annotations
 
 import math
+import weakref
 from dataclasses import dataclass
 from typing import List, Optional, Tuple
 
@@ -138,8 +139,38 @@ class XSAKETransformer(nn.Module):
         pad = -vocab % 64
         if pad:
             w = F.pad(w, (0, 0, 0, pad))
-        logits = F.linear(x, w)[..., :vocab]
+        logits = F.linear(x, w)
+        if pad:
+            logits = _VocabView.apply(logits, vocab)
         return logits, attn
+
+
+# Gradient buffers written by _CrossEntropy.backward over whole padded rows (zeros past the
+# vocabulary), keyed by data pointer until _VocabView.backward takes them (weakly held: an
+# entry disappears with its buffer).
+_PADDED_GRADS: "weakref.WeakValueDictionary" = weakref.WeakValueDictionary()
+
+
+class _VocabView(torch.autograd.Function):
+    """logits[..., :vocab] of the padded logits.  Its backward hands a gradient that already
+    spans the padded rows (the fused cross entropy's) to the GEMM as it is, instead of a zero
+    fill of the padded shape plus a strided copy (two passes over ~3 GB per step)."""
+
+    @staticmethod
+    def forward(ctx, padded, vocab):
+        ctx.padded_shape = padded.shape
+        return padded[..., :vocab]
+
+    @staticmethod
+    def backward(ctx, g):
+        base = g._base
+        if base is not None and _PADDED_GRADS.pop(base.data_ptr(), None) is base and \
+                g.data_ptr() == base.data_ptr() and base.numel() == math.prod(ctx.padded_shape) and \
+                g.stride()[-2] == ctx.padded_shape[-1]:
+            return base.view(ctx.padded_shape), None
+        out = g.new_zeros(ctx.padded_shape)
+        out[..., :g.shape[-1]] = g
+        return out, None
 
 
 class _CrossEntropy(torch.autograd.Function):
@@ -170,6 +201,8 @@ class _CrossEntropy(torch.autograd.Function):
         _lib.check(_lib.load().xsake_xent_bwd(
             dev.xsake_dtype(logits), rows, vocab, ld, logits.data_ptr(), targets.data_ptr(), ctx.ignore_index,
             lse.data_ptr(), coef.data_ptr(), buf.data_ptr(), dev.stream_ptr()))
+        if ld > vocab:
+            _PADDED_GRADS[buf.data_ptr()] = buf
         return buf[:, :vocab], None, None
 
 
