@@ -399,13 +399,13 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             mbar_arrive(&bars->s_free);
             // The chunk's -lse*log2e and Dl came with its TMA copies.
             if (!warp_mbar_wait(&bars->ring_full[st], (g / kKvStages) & 1, abort)) { ok = false; break; }
-            // The previous chunk's accumulation must be done reading P^T / dS^T.
-            if (g > 0 && !warp_mbar_wait(&bars->p_free, (g - 1) & 1, abort)) { ok = false; break; }
             const bool act = (e & f_active) != 0;    // warp-uniform (a warp is inside one half)
             const bool dg = (e & f_diag) != 0;
+            uint32_t ppa[2][16], pda[2][16];   // P^T and dS^T of this row, bf16 pairs
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              uint32_t pp[16], pd[16];
+              uint32_t* pp = ppa[hh];
+              uint32_t* pd = pda[hh];
               if (act) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
@@ -433,8 +433,14 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
 #pragma unroll
                 for (int q = 0; q < 16; ++q) pp[q] = pd[q] = 0u;
               }
-              store_sw128_half(ptrow, rsw, hh, pp);
-              store_sw128_half(dsrow, rsw, hh, pd);
+            }
+            // Computed into registers first: the wait for the previous chunk's accumulation to
+            // release P^T / dS^T overlaps the exponentials above.
+            if (g > 0 && !warp_mbar_wait(&bars->p_free, (g - 1) & 1, abort)) { ok = false; break; }
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              store_sw128_half(ptrow, rsw, hh, ppa[hh]);
+              store_sw128_half(dsrow, rsw, hh, pda[hh]);
             }
             fence_proxy_async_smem();
             tc_fence_before();
@@ -680,12 +686,12 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             XSAKE_TMEM_WAIT_LD32((dr + 32));
             tc_fence_before();
             mbar_arrive(&bars->s_free);
-            if (g > 0 && !warp_mbar_wait(&bars->p_free, (g - 1) & 1, abort)) { ok = false; break; }
             const bool act = (e & f_active) != 0;    // warp-uniform
             const bool dg = (e & f_diag) != 0;
+            uint32_t pda[2][16];   // dS of this row, bf16 pairs
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-              uint32_t pd[16];
+              uint32_t* pd = pda[hh];
               if (act) {
 #pragma unroll
                 for (int q = 0; q < 16; ++q) {
@@ -705,8 +711,12 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
 #pragma unroll
                 for (int q = 0; q < 16; ++q) pd[q] = 0u;
               }
-              store_sw128_half(dsrow, rsw, hh, pd);
             }
+            // Computed into registers first: the wait for the previous chunk's dQ MMA to release
+            // dS overlaps the exponentials above.
+            if (g > 0 && !warp_mbar_wait(&bars->p_free, (g - 1) & 1, abort)) { ok = false; break; }
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) store_sw128_half(dsrow, rsw, hh, pda[hh]);
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&bars->p_full);
