@@ -345,7 +345,7 @@ def run_attention(args, dist, rank, world, local):
                        "parallelism": f"weak, {world} rank(s) x batch {B}, no collective"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "peak_source": f"bf16_tflops ({peak_kind}, burst)",
-                         "kernel": "tc_fwd_pair_kernel", "kernel_ms": kernel_ms, "traffic": _traffic("attn")},
+                         "kernel": "tc_fwd_kernel (unit pairing)", "kernel_ms": kernel_ms, "traffic": _traffic("attn")},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": 3 * B * H * S * D * 2, "d2h_bytes_per_step": B * H * S * D * 2,
                     "steps": e2e_steps, "api": "xsake_b200.sparse_attention.sparse_attention_pallas",

@@ -135,6 +135,22 @@ def test_bf16_mask_per_unit():
     _bf16_case(2, 3, 512, 64, 64, False, m, seed=35)
 
 
+def test_bf16_dense_mask_several_units():
+    # A dense causal mask leaves (almost) nothing masked in query-chunk pairs: the plan keeps the
+    # query-chunk pairing even with several units sharing the mask.
+    _bf16_case(2, 2, 512, 64, 64, True, np.ones((8, 8), bool), seed=36)
+
+
+def test_forward_pairing_follows_the_mask():
+    # Header word 24 of the plan (H_FWD_PAIR): unit pairing for HADS masks shared by 4 units,
+    # query-chunk pairing for one unit per mask and for a dense causal mask.
+    sa = _sa()
+    hads = oh.dummy_hads_profile(12, 4096, 64, causal=True, global_blocks=1).block_masks
+    for m, B, want in [(hads, 4, 1), (hads, 1, 0), (np.ones((64, 64), bool), 4, 0)]:
+        cm = sa.compile_block_mask(m, B, 12, 4096, 64, True)
+        assert int(cm.plan.view(torch.int32)[24].item()) == want, (B, want)
+
+
 def test_bf16_bshd_layout_and_scale():
     prof = oh.dummy_hads_profile(4, 256, 64, causal=True)
     _bf16_case(2, 4, 256, 64, 64, True, prof.block_masks, seed=40, layout="bshd", scale=0.2)

@@ -37,10 +37,12 @@
 // The running max is only moved when it grows by more than 2^8 (rescaling O in TMEM is then
 // rare); exp2 runs on MUFU for 3/4 of the elements and on a cubic polynomial for the rest.
 //
-// Two kernels share this structure.  tc_fwd_kernel (above) pairs query chunks 2t, 2t+1 of one
-// (b, h) and is used when every (b, h) has its own mask.  tc_fwd_pair_kernel pairs the same
-// query chunk of two (b, h) units that share a mask (a mask broadcast over the batch or the
-// heads, the usual HADS case) and is used whenever two such units exist; see its comment.
+// Two pairings share this structure (tile_roles and pair_roles, one kernel, tc_fwd_kernel, which
+// runs the one the compiled plan names in its header word H_FWD_PAIR).  tile_roles pairs query
+// chunks 2t, 2t+1 of one (b, h).  pair_roles pairs the same query chunk of two (b, h) units that
+// share a mask (a mask broadcast over the batch or the heads, the usual HADS case); the plan
+// compiler picks it when such units exist and the query-chunk pairing would leave more than 12%
+// of its 64-row halves masked out (see the comment above PItem).
 #include "attn_common.cuh"
 #include "sm100.cuh"
 
@@ -151,455 +153,420 @@ __device__ __forceinline__ int32_t entry_at(const int32_t* entries, const W& w, 
   return __shfl_sync(0xffffffffu, held, i - base);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-              const __grid_constant__ CUtensorMap tmV, const TcParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
-  volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
-  volatile int* plan_ok = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
-  volatile int* item_slots = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);   // [tile][slot]
+// State the role functions share: set up once per CTA by tc_fwd_kernel.
+struct FwdCtx {
+  uint8_t* smem;
+  Bars* bars;
+  volatile int* abort;
+  volatile int* item_slots;   // [tile worker][slot]
+  uint32_t tmem;
+  const int32_t* rowptr;
+  const int32_t* entries;
+};
+
+// Roles of the query-chunk pairing: a work item is query chunks 2t, 2t+1 of one (b, h).
+__device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                                           const CUtensorMap& tmV, const TcParams& p, const FwdCtx& c) {
+  uint8_t* smem = c.smem;
+  Bars* bars = c.bars;
+  volatile int* abort = c.abort;
+  volatile int* item_slots = c.item_slots;
+  const uint32_t tmem = c.tmem;
+  const int32_t* rowptr = c.rowptr;
+  const int32_t* entries = c.entries;
   const AttnArgs& a = p.a;
   const PlanLayout& L = a.L;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    *abort = 0;
-    *plan_ok = plan_matches(a) && a.plan[H_HAS_CSR] == 1;
-    if (!*plan_ok) record_device_error(DEV_ERR_PLAN, 10);
-    for (int s = 0; s < 2; ++s) {
-      for (int t = 0; t < 2; ++t) {
-        mbar_init(&bars->item_full[t][s], 1);
-        mbar_init(&bars->item_empty[t][s], kItemReaders);
-        mbar_init(&bars->q_full[t][s], 1);
-        mbar_init(&bars->q_empty[t][s], 1);
-      }
-      mbar_init(&bars->o_free[s], 128);
-      for (int b = 0; b < 2; ++b) mbar_init(&bars->o_done[s][b], 1);
-      for (int b = 0; b < 3; ++b) mbar_init(&bars->p_full[s][b], 128);
-      for (int b = 0; b < 3; ++b) mbar_init(&bars->s_full[s][b], 1);
-    }
-    for (int t = 0; t < 2; ++t)
-      for (int s = 0; s < kStages; ++s) {
-        mbar_init(&bars->kv_full[t][s], 1);
-        mbar_init(&bars->kv_empty[t][s], 1);
-      }
-    mbar_init(&bars->drain, 2);
-    fence_barrier_init();
-    fence_proxy_async_smem();
-  }
-  if (warp == 8 && lane == 0) {
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmV);
-  }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const int32_t* rowptr = a.plan + L.f_rowptr_off;
-  const int32_t* entries = a.plan + L.f_entries_off;
   const int32_t* items = a.plan + L.f_items_off;
-
-  if (*plan_ok) {
-    if (warp == 8 || warp == 9) {
-      // ------------------------------------------------------------------ scheduler + TMA
-      // One warp per tile (X = warp - 8); the whole warp runs the (uniform) control flow, one
-      // elected lane issues.
-      const int X = warp - 8;
-      volatile int* item_slot = item_slots + 2 * X;
-      uint8_t* kv0 = smem + kOffKV + X * kStages * kStageBytes;
-      uint32_t it = 0, qk = 0;
-      bool ok = true;
-      for (uint32_t k = 0; ok; ++k) {
-        const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_empty[X][slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
-        int idx = 0;
-        if (lane == 0) idx = *abort ? L.nitems : atomicAdd(p.counter, 1);
-        idx = __shfl_sync(0xffffffffu, idx, 0);
-        const int item = idx < L.nitems ? items[idx] : -1;
+  if (warp == 8 || warp == 9) {
+    // ------------------------------------------------------------------ scheduler + TMA
+    // One warp per tile (X = warp - 8); the whole warp runs the (uniform) control flow, one
+    // elected lane issues.
+    const int X = warp - 8;
+    volatile int* item_slot = item_slots + 2 * X;
+    uint8_t* kv0 = smem + kOffKV + X * kStages * kStageBytes;
+    uint32_t it = 0, qk = 0;
+    bool ok = true;
+    for (uint32_t k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!warp_mbar_wait(&bars->item_empty[X][slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+      int idx = 0;
+      if (lane == 0) idx = *abort ? L.nitems : atomicAdd(p.counter, 1);
+      idx = __shfl_sync(0xffffffffu, idx, 0);
+      const int item = idx < L.nitems ? items[idx] : -1;
+      if (elect_one()) {
+        item_slot[slot] = item;
+        mbar_arrive(&bars->item_full[X][slot]);
+      }
+      __syncwarp();
+      if (item < 0) break;
+      const Item w = decode(a, rowptr, item);
+      if (w.n == 0) continue;
+      const int qs = qk % kQSlots;
+      if (!warp_mbar_wait(&bars->q_empty[X][qs], ((qk / kQSlots) & 1) ^ 1, abort)) { ok = false; break; }
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&bars->q_full[X][qs], kQBytes);
+        uint8_t* qbuf = smem + kOffQ + (kQSlots * X + qs) * kQBytes;   // two 64-row boxes
+          tma_load_4d(qbuf, &tmQ, &bars->q_full[X][qs], 0, 128 * w.u, w.h, w.b);
+          tma_load_4d(qbuf + kQBytes / 2, &tmQ, &bars->q_full[X][qs], 0, 128 * w.u + 64, w.h, w.b);
+      }
+      __syncwarp();
+      ++qk;
+      int32_t held = 0;
+      int base = -32;
+      for (int i = 0; i < w.n; ++i, ++it) {
+        const int c = entry_at(entries, w, i, held, base) & kEntryIdxMask;
+        const int st = it % kStages;
+        if (!warp_mbar_wait(&bars->kv_empty[X][st], ((it / kStages) & 1) ^ 1, abort)) { ok = false; break; }
         if (elect_one()) {
-          item_slot[slot] = item;
-          mbar_arrive(&bars->item_full[X][slot]);
+          uint8_t* kbuf = kv0 + st * kStageBytes;
+          mbar_arrive_expect_tx(&bars->kv_full[X][st], kStageBytes);
+          tma_load_4d(kbuf, &tmK, &bars->kv_full[X][st], 0, 64 * c, w.h, w.b);
+          tma_load_4d(kbuf + kKBytes, &tmV, &bars->kv_full[X][st], 0, 64 * c, w.h, w.b);
         }
         __syncwarp();
-        if (item < 0) break;
-        const Item w = decode(a, rowptr, item);
-        if (w.n == 0) continue;
-        const int qs = qk % kQSlots;
-        if (!warp_mbar_wait(&bars->q_empty[X][qs], ((qk / kQSlots) & 1) ^ 1, abort)) { ok = false; break; }
-        if (elect_one()) {
-          mbar_arrive_expect_tx(&bars->q_full[X][qs], kQBytes);
-          tma_load_4d(smem + kOffQ + (kQSlots * X + qs) * kQBytes, &tmQ, &bars->q_full[X][qs], 0, 128 * w.u, w.h,
-                      w.b);
+      }
+    }
+    if (!ok && lane == 0) {
+      fail(abort, 1);
+      // Give copies in flight a bounded chance to land before the CTA exits.
+      for (int s = 0; s < kStages; ++s) {
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&bars->kv_full[X][s], 0) && !mbar_try_wait(&bars->kv_full[X][s], 1) &&
+               global_timer_ns() - t0 < 1000000ull) {
         }
-        __syncwarp();
-        ++qk;
-        int32_t held = 0;
-        int base = -32;
-        for (int i = 0; i < w.n; ++i, ++it) {
-          const int c = entry_at(entries, w, i, held, base) & kEntryIdxMask;
-          const int st = it % kStages;
-          if (!warp_mbar_wait(&bars->kv_empty[X][st], ((it / kStages) & 1) ^ 1, abort)) { ok = false; break; }
-          if (elect_one()) {
-            uint8_t* kbuf = kv0 + st * kStageBytes;
-            mbar_arrive_expect_tx(&bars->kv_full[X][st], kStageBytes);
-            tma_load_4d(kbuf, &tmK, &bars->kv_full[X][st], 0, 64 * c, w.h, w.b);
-            tma_load_4d(kbuf + kKBytes, &tmV, &bars->kv_full[X][st], 0, 64 * c, w.h, w.b);
-          }
+      }
+    }
+  } else if (warp == 10 || warp == 11) {
+    // ------------------------------------------------------------------ MMA issuers
+    // One warp per tile worker (X = warp - 10).
+    // The whole warp runs the (uniform) control flow; one elected lane issues.  The entries
+    // of the item are visited in order (the plan lists only chunks the tile attends; an entry
+    // without an active flag would be released unused, after its load landed).  QK of step s
+    // goes into S buffer s%3 once PV(s-3) has been issued (which implies the softmax has read
+    // S(s-3)); PV(s-2) is issued right after QK(s), the item's last ones at its end.
+    const int X = warp - 10;
+    volatile int* item_slot = item_slots + 2 * X;
+    const int32_t f_tile = kEntryFlags;
+    const uint32_t tcol = tmem + 256 * X;
+    const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV + X * kStages * kStageBytes), 16, 1024);
+    uint32_t it = 0, qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
+    int pst0 = 0, pst1 = 0, pst2 = 0;   // ring stage of the step in S buffer 0, 1, 2 (registers)
+    auto pstage = [&](uint32_t b) { return b == 0 ? pst0 : (b == 1 ? pst1 : pst2); };
+    bool ok = true;
+    auto issue_pv = [&]() -> bool {
+      const uint32_t s = pvs, pb = s & 1, sbuf = s % 3;
+      if (!warp_mbar_wait(&bars->p_full[X][sbuf], (s / 3) & 1, abort)) return false;
+      const bool first = (s == item_first);
+      if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
+      tc_fence_after();
+      const int st = pstage(sbuf);
+      if (elect_one()) {
+        const uint64_t vdesc = kdesc0 + (uint64_t)((st * kStageBytes + kKBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)   // O += P V, P = 16 keys per 8 TMEM columns
+          mma_bf16_ts(tcol + 192, tcol + 64 * sbuf + 8 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
+                      (first && kk == 0) ? 0u : 1u);
+        mma_commit(&bars->o_done[X][pb]);
+        mma_commit(&bars->kv_empty[X][st]);
+      }
+      __syncwarp();
+      ++pvs;
+      return true;
+    };
+    for (uint32_t k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
+      const int item = item_slot[slot];
+      __syncwarp();
+      if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
+      __syncwarp();
+      if (item < 0) break;
+      const Item w = decode(a, rowptr, item);
+      if (w.n == 0) continue;
+      const int qs = qk % kQSlots;
+      if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
+      ++qk;
+      const uint64_t qdesc = sw128_desc(smem_u32(smem + kOffQ + (kQSlots * X + qs) * kQBytes), 16, 1024);
+      item_first = steps;
+      int last_used = -1;
+      for (int b0 = 0; b0 < w.n; b0 += 32) {
+        const int j = b0 + lane;
+        const uint32_t own = __ballot_sync(0xffffffffu, j < w.n && (entries[w.e0 + j] & f_tile) != 0);
+        if (own) last_used = b0 + 31 - __clz(own);
+      }
+      int32_t held = 0;
+      int base = -32;
+      for (int i = 0; i < w.n && ok; ++i, ++it) {
+        const int32_t e = entry_at(entries, w, i, held, base);
+        const int st = it % kStages;
+        if (!(e & f_tile)) {
+          // Pending PVs hold ring stages: issue them before waiting on an entry that is not used.
+          while (ok && pvs < steps) ok = issue_pv();
+          if (!ok || !warp_mbar_wait(&bars->kv_full[X][st], (it / kStages) & 1, abort)) { ok = false; break; }
+          if (elect_one()) mbar_arrive(&bars->kv_empty[X][st]);
           __syncwarp();
+          continue;
         }
-      }
-      if (!ok && lane == 0) {
-        fail(abort, 1);
-        // Give copies in flight a bounded chance to land before the CTA exits.
-        for (int s = 0; s < kStages; ++s) {
-          const uint64_t t0 = global_timer_ns();
-          while (!mbar_try_wait(&bars->kv_full[X][s], 0) && !mbar_try_wait(&bars->kv_full[X][s], 1) &&
-                 global_timer_ns() - t0 < 1000000ull) {
-          }
-        }
-      }
-    } else if (warp == 10 || warp == 11) {
-      // ------------------------------------------------------------------ MMA issuers
-      // One warp per tile worker (X = warp - 10).
-      // The whole warp runs the (uniform) control flow; one elected lane issues.  The entries
-      // of the item are visited in order (the plan lists only chunks the tile attends; an entry
-      // without an active flag would be released unused, after its load landed).  QK of step s
-      // goes into S buffer s%3 once PV(s-3) has been issued (which implies the softmax has read
-      // S(s-3)); PV(s-2) is issued right after QK(s), the item's last ones at its end.
-      const int X = warp - 10;
-      volatile int* item_slot = item_slots + 2 * X;
-      const int32_t f_tile = kEntryFlags;
-      const uint32_t tcol = tmem + 256 * X;
-      const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV + X * kStages * kStageBytes), 16, 1024);
-      uint32_t it = 0, qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
-      int pst0 = 0, pst1 = 0, pst2 = 0;   // ring stage of the step in S buffer 0, 1, 2 (registers)
-      auto pstage = [&](uint32_t b) { return b == 0 ? pst0 : (b == 1 ? pst1 : pst2); };
-      bool ok = true;
-      auto issue_pv = [&]() -> bool {
-        const uint32_t s = pvs, pb = s & 1, sbuf = s % 3;
-        if (!warp_mbar_wait(&bars->p_full[X][sbuf], (s / 3) & 1, abort)) return false;
-        const bool first = (s == item_first);
-        if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
+        // One batch per step: PV(steps - kPvLag) of this item, then QK(steps) (which needs
+        // PV(steps - 3) issued, so kPvLag <= 3), after one combined wait for both operands.
+        while (ok && pvs + kPvLag < steps) ok = issue_pv();
+        if (!ok) break;
+        const bool pv_now = pvs + kPvLag == steps;
+        const uint32_t ps = pvs, psb = ps % 3;
+        const bool pv_first = pv_now && ps == item_first;
+        if (pv_first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) { ok = false; break; }
+        if (!warp_mbar_wait2(&bars->kv_full[X][st], (it / kStages) & 1, &bars->p_full[X][psb], (ps / 3) & 1,
+                             pv_now, abort)) { ok = false; break; }
+        const uint32_t sb = steps % 3;
         tc_fence_after();
-        const int st = pstage(sbuf);
         if (elect_one()) {
-          const uint64_t vdesc = kdesc0 + (uint64_t)((st * kStageBytes + kKBytes) >> 4);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)   // O += P V, P = 16 keys per 8 TMEM columns
-            mma_bf16_ts(tcol + 192, tcol + 64 * sbuf + 8 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
-                        (first && kk == 0) ? 0u : 1u);
-          mma_commit(&bars->o_done[X][pb]);
-          mma_commit(&bars->kv_empty[X][st]);
-        }
-        __syncwarp();
-        ++pvs;
-        return true;
-      };
-      for (uint32_t k = 0; ok; ++k) {
-        const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
-        const int item = item_slot[slot];
-        __syncwarp();
-        if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
-        __syncwarp();
-        if (item < 0) break;
-        const Item w = decode(a, rowptr, item);
-        if (w.n == 0) continue;
-        const int qs = qk % kQSlots;
-        if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
-        ++qk;
-        const uint64_t qdesc = sw128_desc(smem_u32(smem + kOffQ + (kQSlots * X + qs) * kQBytes), 16, 1024);
-        item_first = steps;
-        int last_used = -1;
-        for (int b0 = 0; b0 < w.n; b0 += 32) {
-          const int j = b0 + lane;
-          const uint32_t own = __ballot_sync(0xffffffffu, j < w.n && (entries[w.e0 + j] & f_tile) != 0);
-          if (own) last_used = b0 + 31 - __clz(own);
-        }
-        int32_t held = 0;
-        int base = -32;
-        for (int i = 0; i < w.n && ok; ++i, ++it) {
-          const int32_t e = entry_at(entries, w, i, held, base);
-          const int st = it % kStages;
-          if (!(e & f_tile)) {
-            // Pending PVs hold ring stages: issue them before waiting on an entry that is not used.
-            while (ok && pvs < steps) ok = issue_pv();
-            if (!ok || !warp_mbar_wait(&bars->kv_full[X][st], (it / kStages) & 1, abort)) { ok = false; break; }
-            if (elect_one()) mbar_arrive(&bars->kv_empty[X][st]);
-            __syncwarp();
-            continue;
-          }
-          // One batch per step: PV(steps - kPvLag) of this item, then QK(steps) (which needs
-          // PV(steps - 3) issued, so kPvLag <= 3), after one combined wait for both operands.
-          while (ok && pvs + kPvLag < steps) ok = issue_pv();
-          if (!ok) break;
-          const bool pv_now = pvs + kPvLag == steps;
-          const uint32_t ps = pvs, psb = ps % 3;
-          const bool pv_first = pv_now && ps == item_first;
-          if (pv_first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) { ok = false; break; }
-          if (!warp_mbar_wait2(&bars->kv_full[X][st], (it / kStages) & 1, &bars->p_full[X][psb], (ps / 3) & 1,
-                               pv_now, abort)) { ok = false; break; }
-          const uint32_t sb = steps % 3;
-          tc_fence_after();
-          if (elect_one()) {
-            if (pv_now) {
-              const int pst = pstage(psb);
-              const uint64_t vdesc = kdesc0 + (uint64_t)((pst * kStageBytes + kKBytes) >> 4);
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_bf16_ts(tcol + 192, tcol + 64 * psb + 8 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
-                            (pv_first && kk == 0) ? 0u : 1u);
-              mma_commit(&bars->o_done[X][ps & 1]);
-              mma_commit(&bars->kv_empty[X][pst]);
-            }
-            const uint64_t kdesc = kdesc0 + (uint64_t)((st * kStageBytes) >> 4);
+          if (pv_now) {
+            const int pst = pstage(psb);
+            const uint64_t vdesc = kdesc0 + (uint64_t)((pst * kStageBytes + kKBytes) >> 4);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_ss(tcol + 64 * sb, qdesc + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
-            mma_commit(&bars->s_full[X][sb]);
-            if (i == last_used) mma_commit(&bars->q_empty[X][qs]);
+              mma_bf16_ts(tcol + 192, tcol + 64 * psb + 8 * kk, vdesc + (uint64_t)((2048 * kk) >> 4), kIdescPV,
+                          (pv_first && kk == 0) ? 0u : 1u);
+            mma_commit(&bars->o_done[X][ps & 1]);
+            mma_commit(&bars->kv_empty[X][pst]);
           }
-          __syncwarp();
-          if (pv_now) ++pvs;
-          pst0 = sb == 0 ? st : pst0;
-          pst1 = sb == 1 ? st : pst1;
-          pst2 = sb == 2 ? st : pst2;
-          ++steps;
+          const uint64_t kdesc = kdesc0 + (uint64_t)((st * kStageBytes) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_ss(tcol + 64 * sb, qdesc + 2 * kk, kdesc + 2 * kk, kIdescQK, kk > 0 ? 1u : 0u);
+          mma_commit(&bars->s_full[X][sb]);
+          if (i == last_used) mma_commit(&bars->q_empty[X][qs]);
         }
-        if (!ok) break;
-        while (ok && pvs < steps) ok = issue_pv();
-        if (!ok) break;
-        if (last_used < 0) {           // this tile had nothing in the item: release its Q share
-          if (elect_one()) mbar_arrive(&bars->q_empty[X][qs]);
-          __syncwarp();
-        }
-        if (steps > item_first) ++titems;
+        __syncwarp();
+        if (pv_now) ++pvs;
+        pst0 = sb == 0 ? st : pst0;
+        pst1 = sb == 1 ? st : pst1;
+        pst2 = sb == 2 ? st : pst2;
+        ++steps;
       }
-      if (!ok && lane == 0) fail(abort, 3);
-      // Drain: no MMA may be in flight when TMEM is released.
-      if (elect_one()) mma_commit(&bars->drain);
-      __syncwarp();
-      if (lane == 0) {
-        const uint64_t t0 = global_timer_ns();
-        while (!mbar_try_wait(&bars->drain, 0) && global_timer_ns() - t0 < kWaitLimitNs) {
-        }
+      if (!ok) break;
+      while (ok && pvs < steps) ok = issue_pv();
+      if (!ok) break;
+      if (last_used < 0) {           // this tile had nothing in the item: release its Q share
+        if (elect_one()) mbar_arrive(&bars->q_empty[X][qs]);
+        __syncwarp();
       }
-      __syncwarp();
-    } else {
-      // ------------------------------------------------------------------ softmax + epilogue
-      const int X = warp >> 2;                 // tile
-      const int row = threadIdx.x & 127;       // TMEM lane
-      const int half = row >> 6;
-      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-      const uint32_t tcol = tmem + 256 * X;
-      volatile int* item_slot = item_slots + 2 * X;
-      const int32_t f_tile = kEntryFlags;
-      const int32_t f_active = half ? kFlagActive1 : kFlagActive0;
-      const int32_t f_diag = half ? kFlagDiag1 : kFlagDiag0;
-      const int diag_lim = row & 63;
-      uint64_t* s_full = bars->s_full[X];
-      uint64_t* p_full = bars->p_full[X];
-      uint64_t* o_done = bars->o_done[X];
-      uint64_t* o_free = &bars->o_free[X];
-      uint32_t it = 0, sb_c = 0, ph_c = 0;   // step count, its S buffer (it % 3) and phase ((it / 3) & 1)
-      bool s_ready = false;                  // S of step `it` already seen complete by every lane
-      bool ok = true;
-      for (uint32_t k = 0; ok; ++k) {
-        const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
-        const int item = item_slot[slot];
-        mbar_arrive(&bars->item_empty[X][slot]);
-        if (item < 0) break;
-        const Item w = decode(a, rowptr, item);
-        float m = -INFINITY, l = 0.f;
-        int nsteps = 0;
-        // The item's entries, 32 at a time: a ballot marks them and a shuffle hands each one out.
-        for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
-          const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
-          uint32_t own = __ballot_sync(0xffffffffu, (eb & f_tile) != 0);
-          while (own) {
-            const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
-            own &= own - 1;
-            ++nsteps;
-            const uint32_t sb = sb_c;
-            if (!s_ready && !warp_mbar_wait(&s_full[sb], ph_c, abort)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t sr[64];
-            XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
-            XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
-            // Probe the next step's S while the load is in flight (non-blocking; the QKs run
-            // ahead, so it has usually landed): a complete phase seen by every lane saves the
-            // next wait.  The probe has acquire semantics, like the wait it replaces.
-            const bool next_done = mbar_test_wait(&s_full[sb_c == 2 ? 0 : sb_c + 1], sb_c == 2 ? ph_c ^ 1u : ph_c);
-            XSAKE_TMEM_WAIT_LD32(sr);
-            XSAKE_TMEM_WAIT_LD32((sr + 32));
-            s_ready = __all_sync(0xffffffffu, next_done);
-            uint32_t pk[32];
-            if (e & f_active) {
-              float* x = reinterpret_cast<float*>(sr);   // raw scores
-              if (e & f_diag) {                          // warp-uniform: token-level causal cut
-#pragma unroll
-                for (int j = 0; j < 64; ++j)
-                  if (j > diag_lim) x[j] = -INFINITY;
-              }
-              // Row max of the raw scores: a depth-4 tree of 3-input maxes.
-              float t1[22];
-#pragma unroll
-              for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
-              t1[21] = x[63];
-              float t2[8];
-#pragma unroll
-              for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
-              t2[7] = t1[21];
-              const float mraw =
-                  fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
-              const float mx = mraw * p.scale_log2;       // log2 units (scale > 0)
-              const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
-              if (m == -INFINITY) m = mx;
-              // TMEM loads/stores are warp-collective: the whole warp rescales when any row must.
-              if (__any_sync(0xffffffffu, need)) {
-                // O holds PV of earlier chunks: wait for the last one, then rescale in TMEM.
-                if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
-                tc_fence_after();
-                const float alpha = need ? ex2(m - mx) : 1.0f;
-                uint32_t orow[32];
-#pragma unroll
-                for (int hcol = 0; hcol < 2; ++hcol) {
-                  XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
-                  XSAKE_TMEM_WAIT_LD32(orow);
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
-                  XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
-                }
-                tmem_wait_st();
-                if (need) {
-                  l *= alpha;
-                  m = mx;
-                }
-              }
-              const float msub = (m == -INFINITY) ? 0.f : m;   // no live score yet: every x is -inf
-              // p = 2^(s*scale*log2e - m): one packed FMA per pair; 2 of every 8 pairs go through
-              // the polynomial exp2 on the FMA/ALU pipes, the rest through MUFU ex2.
-              const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
-              uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float x0, x1, p0, p1;
-                upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
-                if ((j & 7) < 2) {
-                  exp2_poly2(x0, x1, p0, p1);
-                } else {
-                  p0 = ex2(x0);
-                  p1 = ex2(x1);
-                }
-                acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
-                __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-                pk[j] = *reinterpret_cast<uint32_t*>(&pb);
-              }
-              float s0, s1;
-              upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
-              l += s0 + s1;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) pk[j] = 0u;
-            }
-            // P over the first 32 columns of the S buffer this thread has just read (its own row).
-            XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&p_full[sb]);
-            ++it;
-            if (++sb_c == 3) {
-              sb_c = 0;
-              ph_c ^= 1;
-            }
-          }
-        }
-        if (!ok) break;
-        // ---------------------------------------------------------------- epilogue
-        const int tok = 128 * w.u + row;
-        const bool valid = tok < a.S;
-        const bool empty = valid && !(l > 0.f);
-        uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + w.b * a.os[0] +
-                                                 w.h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
-        if (nsteps > 0) {
-          // PV(s) completes phase s/2 of o_done[s % 2].  A parity wait for PV(it-1) is only
-          // unambiguous if that barrier's previous phase (PV(it-3)) has completed; the last S
-          // buffer seen (QK(it-1)) only implies PV(it-4).  So wait for PV(it-2) first (its
-          // previous phase, PV(it-4), is known complete), which implies PV(it-3), then PV(it-1).
-          // (Inside the loop the rescale at step it is safe: QK(it) implies PV(it-3).)
-          if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
-          if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
-          tc_fence_after();
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-          for (int hcol = 0; hcol < 2; ++hcol) {
-            uint32_t orow[32];
-            XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
-            XSAKE_TMEM_WAIT_LD32(orow);
-            if (valid && !empty) {
-#pragma unroll
-              for (int cc = 0; cc < 4; ++cc) {
-                uint32_t wv[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  __nv_bfloat162 pb = __floats2bfloat162_rn(__uint_as_float(orow[8 * cc + 2 * q]) * inv,
-                                                            __uint_as_float(orow[8 * cc + 2 * q + 1]) * inv);
-                  wv[q] = *reinterpret_cast<uint32_t*>(&pb);
-                }
-                orow_g[4 * hcol + cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-              }
-            }
-          }
-          tc_fence_before();
-          mbar_arrive(o_free);
-        }
-        if (__any_sync(0xffffffffu, empty)) {
-          // Rows with no live score: the reference's finfo.min fill makes them attend uniformly.
-          float2 mine;
-          warp_mean_v(a, w.b, w.h, mine);
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            uint32_t wv[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int src = 4 * cc + q;   // column pair index 0..31
-              __nv_bfloat162 pb = __floats2bfloat162_rn(__shfl_sync(0xffffffffu, mine.x, src),
-                                                        __shfl_sync(0xffffffffu, mine.y, src));
-              wv[q] = *reinterpret_cast<uint32_t*>(&pb);
-            }
-            if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-          }
-        }
-        if (valid) a.lse[(int64_t)(w.b * a.H + w.h) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
-      }
-      if (!ok) fail(abort, 4);
+      if (steps > item_first) ++titems;
     }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    if (!ok && lane == 0) fail(abort, 3);
+    // Drain: no MMA may be in flight when TMEM is released.
+    if (elect_one()) mma_commit(&bars->drain);
+    __syncwarp();
+    if (lane == 0) {
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(&bars->drain, 0) && global_timer_ns() - t0 < kWaitLimitNs) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int X = warp >> 2;                 // tile
+    const int row = threadIdx.x & 127;       // TMEM lane
+    const int half = row >> 6;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tcol = tmem + 256 * X;
+    volatile int* item_slot = item_slots + 2 * X;
+    const int32_t f_tile = kEntryFlags;
+    const int32_t f_active = half ? kFlagActive1 : kFlagActive0;
+    const int32_t f_diag = half ? kFlagDiag1 : kFlagDiag0;
+    const int diag_lim = row & 63;
+    uint64_t* s_full = bars->s_full[X];
+    uint64_t* p_full = bars->p_full[X];
+    uint64_t* o_done = bars->o_done[X];
+    uint64_t* o_free = &bars->o_free[X];
+    uint32_t it = 0, sb_c = 0, ph_c = 0;   // step count, its S buffer (it % 3) and phase ((it / 3) & 1)
+    bool s_ready = false;                  // S of step `it` already seen complete by every lane
+    bool ok = true;
+    for (uint32_t k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
+      const int item = item_slot[slot];
+      mbar_arrive(&bars->item_empty[X][slot]);
+      if (item < 0) break;
+      const Item w = decode(a, rowptr, item);
+      float m = -INFINITY, l = 0.f;
+      int nsteps = 0;
+      // The item's entries, 32 at a time: a ballot marks them and a shuffle hands each one out.
+      for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
+        const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
+        uint32_t own = __ballot_sync(0xffffffffu, (eb & f_tile) != 0);
+        while (own) {
+          const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
+          own &= own - 1;
+          ++nsteps;
+          const uint32_t sb = sb_c;
+          if (!s_ready && !warp_mbar_wait(&s_full[sb], ph_c, abort)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t sr[64];
+          XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
+          XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
+          // Probe the next step's S while the load is in flight (non-blocking; the QKs run
+          // ahead, so it has usually landed): a complete phase seen by every lane saves the
+          // next wait.  The probe has acquire semantics, like the wait it replaces.
+          const bool next_done = mbar_test_wait(&s_full[sb_c == 2 ? 0 : sb_c + 1], sb_c == 2 ? ph_c ^ 1u : ph_c);
+          XSAKE_TMEM_WAIT_LD32(sr);
+          XSAKE_TMEM_WAIT_LD32((sr + 32));
+          s_ready = __all_sync(0xffffffffu, next_done);
+          uint32_t pk[32];
+          if (e & f_active) {
+            float* x = reinterpret_cast<float*>(sr);   // raw scores
+            if (e & f_diag) {                          // warp-uniform: token-level causal cut
+#pragma unroll
+              for (int j = 0; j < 64; ++j)
+                if (j > diag_lim) x[j] = -INFINITY;
+            }
+            // Row max of the raw scores: a depth-4 tree of 3-input maxes.
+            float t1[22];
+#pragma unroll
+            for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+            t1[21] = x[63];
+            float t2[8];
+#pragma unroll
+            for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
+            t2[7] = t1[21];
+            const float mraw =
+                fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
+            const float mx = mraw * p.scale_log2;       // log2 units (scale > 0)
+            const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
+            if (m == -INFINITY) m = mx;
+            // TMEM loads/stores are warp-collective: the whole warp rescales when any row must.
+            if (__any_sync(0xffffffffu, need)) {
+              // O holds PV of earlier chunks: wait for the last one, then rescale in TMEM.
+              if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
+              tc_fence_after();
+              const float alpha = need ? ex2(m - mx) : 1.0f;
+              uint32_t orow[32];
+#pragma unroll
+              for (int hcol = 0; hcol < 2; ++hcol) {
+                XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
+                XSAKE_TMEM_WAIT_LD32(orow);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
+                XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
+              }
+              tmem_wait_st();
+              if (need) {
+                l *= alpha;
+                m = mx;
+              }
+            }
+            const float msub = (m == -INFINITY) ? 0.f : m;   // no live score yet: every x is -inf
+            // p = 2^(s*scale*log2e - m): one packed FMA per pair; 2 of every 8 pairs go through
+            // the polynomial exp2 on the FMA/ALU pipes, the rest through MUFU ex2.
+            const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
+            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float x0, x1, p0, p1;
+              upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
+              if ((j & 7) < 2) {
+                exp2_poly2(x0, x1, p0, p1);
+              } else {
+                p0 = ex2(x0);
+                p1 = ex2(x1);
+              }
+              acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
+              __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+              pk[j] = *reinterpret_cast<uint32_t*>(&pb);
+            }
+            float s0, s1;
+            upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
+            l += s0 + s1;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) pk[j] = 0u;
+          }
+          // P over the first 32 columns of the S buffer this thread has just read (its own row).
+          XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&p_full[sb]);
+          ++it;
+          if (++sb_c == 3) {
+            sb_c = 0;
+            ph_c ^= 1;
+          }
+        }
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------------- epilogue
+      const int tok = 128 * w.u + row;
+      const bool valid = tok < a.S;
+      const bool empty = valid && !(l > 0.f);
+      uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + w.b * a.os[0] +
+                                               w.h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
+      if (nsteps > 0) {
+        // PV(s) completes phase s/2 of o_done[s % 2].  A parity wait for PV(it-1) is only
+        // unambiguous if that barrier's previous phase (PV(it-3)) has completed; the last S
+        // buffer seen (QK(it-1)) only implies PV(it-4).  So wait for PV(it-2) first (its
+        // previous phase, PV(it-4), is known complete), which implies PV(it-3), then PV(it-1).
+        // (Inside the loop the rescale at step it is safe: QK(it) implies PV(it-3).)
+        if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
+        if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int hcol = 0; hcol < 2; ++hcol) {
+          uint32_t orow[32];
+          XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
+          XSAKE_TMEM_WAIT_LD32(orow);
+          if (valid && !empty) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              uint32_t wv[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                __nv_bfloat162 pb = __floats2bfloat162_rn(__uint_as_float(orow[8 * cc + 2 * q]) * inv,
+                                                          __uint_as_float(orow[8 * cc + 2 * q + 1]) * inv);
+                wv[q] = *reinterpret_cast<uint32_t*>(&pb);
+              }
+              orow_g[4 * hcol + cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(o_free);
+      }
+      if (__any_sync(0xffffffffu, empty)) {
+        // Rows with no live score: the reference's finfo.min fill makes them attend uniformly.
+        float2 mine;
+        warp_mean_v(a, w.b, w.h, mine);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int src = 4 * cc + q;   // column pair index 0..31
+            __nv_bfloat162 pb = __floats2bfloat162_rn(__shfl_sync(0xffffffffu, mine.x, src),
+                                                      __shfl_sync(0xffffffffu, mine.y, src));
+            wv[q] = *reinterpret_cast<uint32_t*>(&pb);
+          }
+          if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+      }
+      if (valid) a.lse[(int64_t)(w.b * a.H + w.h) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
+    }
+    if (!ok) fail(abort, 4);
   }
 }
 
+
 // ---------------------------------------------------------------------------------------------
-// Paired-unit forward.  A mask broadcast over the batch (or the heads) gives several (b, h)
-// units the same chunk lists.  A work item of this kernel is one 64-row query chunk j of TWO
+// Unit pairing.  A mask broadcast over the batch (or the heads) gives several (b, h)
+// units the same chunk lists.  A work item of this pairing is one 64-row query chunk j of TWO
 // such units u0, u1: every step is one 64-key chunk c that chunk j attends, computed for both
-// units at once, so both halves of every step do useful work.  The kernel above pairs query
-// chunks 2t and 2t+1 of ONE unit instead and walks the union of their lists; on HADS masks the
-// two lists differ in their random long-range picks and 23% of its half-steps are masked out.
+// units at once, so both halves of every step do useful work.  The query-chunk pairing walks
+// the union of two chunks' lists instead; on HADS masks the two lists differ in their random
+// long-range picks and 23% of its half-steps are masked out.  The price of this pairing is the
+// M=64 MMAs (about the tensor time of M=128 ones for half the rows) and twice the K/V loads per
+// step: measured, it wins at 67-80% useful half-steps (bigbird, HADS, local windows: 3-8%) and
+// loses 7% on a dense causal mask (98.5%).
 //
 // The two units' scores and outputs are M=64 accumulators interleaved in TMEM: unit u0's row r
 // sits in lane 32*(r/16) + r%16, unit u1's in the same lane + 16, so each softmax warp holds 16
@@ -608,7 +575,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
 // the first 32 columns of the unit's scores, O += P V (M=64, A read from the same TMEM lanes as
 // the accumulator).  A ring slot holds one unit's K and V chunk; a step takes two consecutive
 // slots (u0's, then u1's).  Roles, barriers, the scheduler, bounded waits and the softmax
-// arithmetic are those of tc_fwd_kernel.  Items are taken in descending j (longest lists first
+// arithmetic are those of the query-chunk pairing.  Items are taken in descending j (longest lists first
 // under a causal mask).  With an odd number of units per mask the last unit of each group runs
 // alone: its partner lanes are masked out and its second slot is released without a load.
 struct PItem {
@@ -664,9 +631,396 @@ constexpr int kPairKStages = 2;           // K ring (both units' K chunks per st
 constexpr int kPairVStages = 3;           // V ring, released by PV
 static_assert(kPairKStages + kPairVStages <= kStages, "the pair rings reuse the K/V ring's shared memory");
 
+// Roles of the unit pairing (see the comment above PItem).
+__device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtensorMap& tmK,
+                                           const CUtensorMap& tmV, const TcParams& p, const FwdCtx& c) {
+  uint8_t* smem = c.smem;
+  Bars* bars = c.bars;
+  volatile int* abort = c.abort;
+  volatile int* item_slots = c.item_slots;
+  const uint32_t tmem = c.tmem;
+  const int32_t* rowptr = c.rowptr;
+  const int32_t* entries = c.entries;
+  const AttnArgs& a = p.a;
+  const PlanLayout& L = a.L;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nitems = pair_items(L, a.B, a.H);
+  if (warp == 8 || warp == 9) {
+    // ------------------------------------------------------------------ scheduler + TMA
+    const int X = warp - 8;
+    volatile int* item_slot = item_slots + 2 * X;
+    uint8_t* kv0 = smem + kOffKV + X * kStages * kStageBytes;
+    uint32_t it = 0, qk = 0;
+    bool ok = true;
+    for (uint32_t k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!warp_mbar_wait(&bars->item_empty[X][slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+      int idx = 0;
+      if (lane == 0) idx = *abort ? nitems : atomicAdd(p.counter, 1);
+      idx = __shfl_sync(0xffffffffu, idx, 0);
+      const int item = idx < nitems ? idx : -1;
+      if (elect_one()) {
+        item_slot[slot] = item;
+        mbar_arrive(&bars->item_full[X][slot]);
+      }
+      __syncwarp();
+      if (item < 0) break;
+      const PItem w = decode_pair(a, rowptr, item);
+      const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
+      int last = -1;
+      if (count_steps(entries, w.e0, w.n, fa, last) == 0) continue;
+      const int qs = qk % kQSlots;
+      if (!warp_mbar_wait(&bars->q_empty[X][qs], ((qk / kQSlots) & 1) ^ 1, abort)) { ok = false; break; }
+      if (elect_one()) {
+        uint8_t* qbuf = smem + kOffQ + (kQSlots * X + qs) * kQBytes;
+        mbar_arrive_expect_tx(&bars->q_full[X][qs], w.solo ? kQBytes / 2 : kQBytes);
+        tma_load_4d(qbuf, &tmQ, &bars->q_full[X][qs], 0, 64 * w.j, w.h0, w.b0);
+        if (!w.solo) tma_load_4d(qbuf + kQBytes / 2, &tmQ, &bars->q_full[X][qs], 0, 64 * w.j, w.h1, w.b1);
+      }
+      __syncwarp();
+      ++qk;
+      // K of step s goes out before V of step s-1: V(s-1) waits for PV(s-4), which the MMA
+      // warp issues only with QK(s-1), so K is never held up behind a V slot.
+      const uint32_t bytes = w.solo ? kKBytes : 2 * kKBytes;
+      auto load_pair = [&](const CUtensorMap* map, int bar, uint8_t* buf, int c) {
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&bars->kv_full[X][bar], bytes);
+          tma_load_4d(buf, map, &bars->kv_full[X][bar], 0, 64 * c, w.h0, w.b0);
+          if (!w.solo) tma_load_4d(buf + kKBytes, map, &bars->kv_full[X][bar], 0, 64 * c, w.h1, w.b1);
+        }
+        __syncwarp();
+      };
+      auto load_v = [&](uint32_t s, int c) -> bool {
+        const int vs = s % kPairVStages;
+        if (!warp_mbar_wait(&bars->kv_empty[X][kPairKStages + vs], ((s / kPairVStages) & 1) ^ 1, abort))
+          return false;
+        load_pair(&tmV, kPairKStages + vs, kv0 + (kPairKStages + vs) * kStageBytes, c);
+        return true;
+      };
+      int32_t held = 0;
+      int base = -32, pend_c = -1;
+      for (int i = 0; i < w.n && ok; ++i) {
+        const int32_t e = entry_at(entries, w, i, held, base);
+        if (!(e & fa)) continue;
+        const int c = e & kEntryIdxMask;
+        const int ks = it % kPairKStages;
+        if (!warp_mbar_wait(&bars->kv_empty[X][ks], ((it / kPairKStages) & 1) ^ 1, abort)) { ok = false; break; }
+        load_pair(&tmK, ks, kv0 + ks * kStageBytes, c);
+        if (pend_c >= 0 && !load_v(it - 1, pend_c)) { ok = false; break; }
+        pend_c = c;
+        ++it;
+      }
+      if (ok && pend_c >= 0 && !load_v(it - 1, pend_c)) ok = false;
+    }
+    if (!ok && lane == 0) {
+      fail(abort, 1);
+      for (int s = 0; s < kStages; ++s) {
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&bars->kv_full[X][s], 0) && !mbar_try_wait(&bars->kv_full[X][s], 1) &&
+               global_timer_ns() - t0 < 1000000ull) {
+        }
+      }
+    }
+  } else if (warp == 10 || warp == 11) {
+    // ------------------------------------------------------------------ MMA issuers
+    // Per step: one combined wait (both units' K/V slots landed, P of step s-3 written), then
+    // PV(s-3) for both units and QK(s) for both units, as in tc_fwd_kernel.
+    const int X = warp - 10;
+    volatile int* item_slot = item_slots + 2 * X;
+    const uint32_t tcol = tmem + 256 * X;
+    const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV + X * kStages * kStageBytes), 16, 1024);
+    uint32_t qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
+    bool solo = false;                  // the current item (PVs never cross an item)
+    bool ok = true;
+    // PV of step s (both units) from V stage s % kPairVStages; the caller has waited for P(s),
+    // V(s) and, on an item's first PV, for the epilogue to have read the previous item's O.
+    auto emit_pv = [&](uint32_t s, bool first) {
+      const uint32_t sbuf = s % 3;
+      const int vs = kPairKStages + (int)(s % kPairVStages);
+      if (elect_one()) {
+        const uint64_t va = kdesc0 + (uint64_t)((vs * kStageBytes) >> 4);
+        const uint64_t vb = va + (uint64_t)(kKBytes >> 4);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_bf16_ts(tcol + 192, tcol + 64 * sbuf + 8 * kk, va + (uint64_t)((2048 * kk) >> 4), kIdescPV64,
+                      (first && kk == 0) ? 0u : 1u);
+        if (!solo) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_ts(tcol + 192 + kLane16, tcol + 64 * sbuf + 8 * kk + kLane16,
+                        vb + (uint64_t)((2048 * kk) >> 4), kIdescPV64, (first && kk == 0) ? 0u : 1u);
+        }
+        mma_commit(&bars->o_done[X][s & 1]);
+        mma_commit(&bars->kv_empty[X][vs]);
+      }
+      __syncwarp();
+    };
+    auto issue_pv = [&]() -> bool {
+      const uint32_t s = pvs;
+      if (!warp_mbar_wait2(&bars->p_full[X][s % 3], (s / 3) & 1, &bars->kv_full[X][kPairKStages + s % kPairVStages],
+                           (s / kPairVStages) & 1, true, abort))
+        return false;
+      const bool first = (s == item_first);
+      if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
+      tc_fence_after();
+      emit_pv(s, first);
+      ++pvs;
+      return true;
+    };
+    for (uint32_t k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
+      const int item = item_slot[slot];
+      __syncwarp();
+      if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
+      __syncwarp();
+      if (item < 0) break;
+      const PItem w = decode_pair(a, rowptr, item);
+      const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
+      int last_used = -1;
+      if (count_steps(entries, w.e0, w.n, fa, last_used) == 0) continue;
+      const int qs = qk % kQSlots;
+      if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
+      ++qk;
+      const uint32_t qaddr = smem_u32(smem + kOffQ + (kQSlots * X + qs) * kQBytes);
+      const uint64_t qda = sw128_desc(qaddr, 16, 1024), qdb = sw128_desc(qaddr + kQBytes / 2, 16, 1024);
+      item_first = steps;
+      solo = w.solo;
+      int32_t held = 0;
+      int base = -32;
+      for (int i = 0; i < w.n && ok; ++i) {
+        const int32_t e = entry_at(entries, w, i, held, base);
+        if (!(e & fa)) continue;
+        const int ks = steps % kPairKStages;
+        while (ok && pvs + kPvLag < steps) ok = issue_pv();
+        if (!ok) break;
+        const bool pv_now = pvs + kPvLag == steps;
+        const uint32_t ps = pvs;
+        const bool pv_first = pv_now && ps == item_first;
+        if (pv_first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) { ok = false; break; }
+        if (!warp_mbar_wait2(&bars->kv_full[X][ks], (steps / kPairKStages) & 1, &bars->p_full[X][ps % 3],
+                             (ps / 3) & 1, pv_now, abort) ||
+            (pv_now && !warp_mbar_wait(&bars->kv_full[X][kPairKStages + ps % kPairVStages],
+                                       (ps / kPairVStages) & 1, abort))) { ok = false; break; }
+        const uint32_t sb = steps % 3;
+        tc_fence_after();
+        if (pv_now) emit_pv(ps, pv_first);
+        if (elect_one()) {
+          const uint64_t ka = kdesc0 + (uint64_t)((ks * kStageBytes) >> 4);
+          const uint64_t kb = ka + (uint64_t)(kKBytes >> 4);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_bf16_ss(tcol + 64 * sb, qda + 2 * kk, ka + 2 * kk, kIdescQK64, kk > 0 ? 1u : 0u);
+          if (!solo) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_bf16_ss(tcol + 64 * sb + kLane16, qdb + 2 * kk, kb + 2 * kk, kIdescQK64, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&bars->s_full[X][sb]);
+          mma_commit(&bars->kv_empty[X][ks]);
+          if (i == last_used) mma_commit(&bars->q_empty[X][qs]);
+        }
+        __syncwarp();
+        if (pv_now) ++pvs;
+        ++steps;
+      }
+      if (!ok) break;
+      while (ok && pvs < steps) ok = issue_pv();
+      if (!ok) break;
+      if (steps > item_first) ++titems;
+    }
+    if (!ok && lane == 0) fail(abort, 3);
+    if (elect_one()) mma_commit(&bars->drain);
+    __syncwarp();
+    if (lane == 0) {
+      const uint64_t t0 = global_timer_ns();
+      while (!mbar_try_wait(&bars->drain, 0) && global_timer_ns() - t0 < kWaitLimitNs) {
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue
+    const int X = warp >> 2;                 // tile worker
+    const bool upper = lane >= 16;           // partner unit's lanes
+    const int r64 = 16 * (warp & 3) + (lane & 15);   // query row within chunk j
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tcol = tmem + 256 * X;
+    volatile int* item_slot = item_slots + 2 * X;
+    uint64_t* s_full = bars->s_full[X];
+    uint64_t* p_full = bars->p_full[X];
+    uint64_t* o_done = bars->o_done[X];
+    uint64_t* o_free = &bars->o_free[X];
+    uint32_t it = 0, sb_c = 0, ph_c = 0;
+    bool s_ready = false;
+    bool ok = true;
+    for (uint32_t k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
+      const int item = item_slot[slot];
+      mbar_arrive(&bars->item_empty[X][slot]);
+      if (item < 0) break;
+      const PItem w = decode_pair(a, rowptr, item);
+      const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
+      const int32_t fd = (w.j & 1) ? kFlagDiag1 : kFlagDiag0;
+      const bool live = !(w.solo && upper);
+      float m = -INFINITY, l = 0.f;
+      int nsteps = 0;
+      for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
+        const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
+        uint32_t own = __ballot_sync(0xffffffffu, (eb & fa) != 0);
+        while (own) {
+          const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
+          own &= own - 1;
+          ++nsteps;
+          const uint32_t sb = sb_c;
+          if (!s_ready && !warp_mbar_wait(&s_full[sb], ph_c, abort)) { ok = false; break; }
+          tc_fence_after();
+          uint32_t sr[64];
+          XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
+          XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
+          const bool next_done = mbar_test_wait(&s_full[sb_c == 2 ? 0 : sb_c + 1], sb_c == 2 ? ph_c ^ 1u : ph_c);
+          XSAKE_TMEM_WAIT_LD32(sr);
+          XSAKE_TMEM_WAIT_LD32((sr + 32));
+          s_ready = __all_sync(0xffffffffu, next_done);
+          uint32_t pk[32];
+          float* x = reinterpret_cast<float*>(sr);   // raw scores
+          // Keys past the token-level causal cut on the diagonal chunk, and every key of a
+          // lane whose unit is absent (a lone unit), are masked.
+          const int lim = !live ? -1 : ((e & fd) ? r64 : 63);
+          if (__any_sync(0xffffffffu, lim < 63)) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j)
+              if (j > lim) x[j] = -INFINITY;
+          }
+          float t1[22];
+#pragma unroll
+          for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+          t1[21] = x[63];
+          float t2[8];
+#pragma unroll
+          for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
+          t2[7] = t1[21];
+          const float mraw =
+              fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
+          const float mx = mraw * p.scale_log2;
+          const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
+          if (m == -INFINITY) m = mx;
+          if (__any_sync(0xffffffffu, need)) {
+            if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
+            tc_fence_after();
+            const float alpha = need ? ex2(m - mx) : 1.0f;
+            uint32_t orow[32];
+#pragma unroll
+            for (int hcol = 0; hcol < 2; ++hcol) {
+              XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
+              XSAKE_TMEM_WAIT_LD32(orow);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
+              XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
+            }
+            tmem_wait_st();
+            if (need) {
+              l *= alpha;
+              m = mx;
+            }
+          }
+          const float msub = (m == -INFINITY) ? 0.f : m;
+          const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
+          uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x0, x1, p0, p1;
+            upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
+            if ((j & 7) < 2) {
+              exp2_poly2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
+            __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+            pk[j] = *reinterpret_cast<uint32_t*>(&pb);
+          }
+          float s0, s1;
+          upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
+          l += s0 + s1;
+          XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&p_full[sb]);
+          ++it;
+          if (++sb_c == 3) {
+            sb_c = 0;
+            ph_c ^= 1;
+          }
+        }
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------------- epilogue
+      const int bb = upper ? w.b1 : w.b0, hh = upper ? w.h1 : w.h0;
+      const int tok = 64 * w.j + r64;
+      const bool valid = live && tok < a.S;
+      const bool empty = valid && !(l > 0.f);
+      uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + bb * a.os[0] +
+                                               hh * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
+      if (nsteps > 0) {
+        // The same two-phase wait for the last PVs as in tc_fwd_kernel.
+        if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
+        if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+        for (int hcol = 0; hcol < 2; ++hcol) {
+          uint32_t orow[32];
+          XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
+          XSAKE_TMEM_WAIT_LD32(orow);
+          if (valid && !empty) {
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              uint32_t wv[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                __nv_bfloat162 pb = __floats2bfloat162_rn(__uint_as_float(orow[8 * cc + 2 * q]) * inv,
+                                                          __uint_as_float(orow[8 * cc + 2 * q + 1]) * inv);
+                wv[q] = *reinterpret_cast<uint32_t*>(&pb);
+              }
+              orow_g[4 * hcol + cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(o_free);
+      }
+      const bool empty_lo = __any_sync(0xffffffffu, empty && !upper);
+      const bool empty_hi = __any_sync(0xffffffffu, empty && upper);
+      if (empty_lo || empty_hi) {
+        // Rows with no live score attend uniformly (the reference's finfo.min fill).
+        float2 mean0 = make_float2(0.f, 0.f), mean1 = make_float2(0.f, 0.f);
+        if (empty_lo) warp_mean_v(a, w.b0, w.h0, mean0);
+        if (empty_hi) warp_mean_v(a, w.b1, w.h1, mean1);
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          uint32_t wv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int src = 4 * cc + q;
+            const float x0 = __shfl_sync(0xffffffffu, mean0.x, src), y0 = __shfl_sync(0xffffffffu, mean0.y, src);
+            const float x1 = __shfl_sync(0xffffffffu, mean1.x, src), y1 = __shfl_sync(0xffffffffu, mean1.y, src);
+            __nv_bfloat162 pb = __floats2bfloat162_rn(upper ? x1 : x0, upper ? y1 : y0);
+            wv[q] = *reinterpret_cast<uint32_t*>(&pb);
+          }
+          if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        }
+      }
+      if (valid) a.lse[(int64_t)(bb * a.H + hh) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
+    }
+    if (!ok) fail(abort, 4);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
-tc_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                   const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+              const __grid_constant__ CUtensorMap tmV, const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
@@ -677,12 +1031,11 @@ tc_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   const AttnArgs& a = p.a;
   const PlanLayout& L = a.L;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nitems = pair_items(L, a.B, a.H);
 
   if (threadIdx.x == 0) {
     *abort = 0;
     *plan_ok = plan_matches(a) && a.plan[H_HAS_CSR] == 1;
-    if (!*plan_ok) record_device_error(DEV_ERR_PLAN, 11);
+    if (!*plan_ok) record_device_error(DEV_ERR_PLAN, 10);
     for (int s = 0; s < 2; ++s) {
       for (int t = 0; t < 2; ++t) {
         mbar_init(&bars->item_full[t][s], 1);
@@ -717,381 +1070,14 @@ tc_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int32_t* rowptr = a.plan + L.f_rowptr_off;
-  const int32_t* entries = a.plan + L.f_entries_off;
 
   if (*plan_ok) {
-    if (warp == 8 || warp == 9) {
-      // ------------------------------------------------------------------ scheduler + TMA
-      const int X = warp - 8;
-      volatile int* item_slot = item_slots + 2 * X;
-      uint8_t* kv0 = smem + kOffKV + X * kStages * kStageBytes;
-      uint32_t it = 0, qk = 0;
-      bool ok = true;
-      for (uint32_t k = 0; ok; ++k) {
-        const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_empty[X][slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
-        int idx = 0;
-        if (lane == 0) idx = *abort ? nitems : atomicAdd(p.counter, 1);
-        idx = __shfl_sync(0xffffffffu, idx, 0);
-        const int item = idx < nitems ? idx : -1;
-        if (elect_one()) {
-          item_slot[slot] = item;
-          mbar_arrive(&bars->item_full[X][slot]);
-        }
-        __syncwarp();
-        if (item < 0) break;
-        const PItem w = decode_pair(a, rowptr, item);
-        const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
-        int last = -1;
-        if (count_steps(entries, w.e0, w.n, fa, last) == 0) continue;
-        const int qs = qk % kQSlots;
-        if (!warp_mbar_wait(&bars->q_empty[X][qs], ((qk / kQSlots) & 1) ^ 1, abort)) { ok = false; break; }
-        if (elect_one()) {
-          uint8_t* qbuf = smem + kOffQ + (kQSlots * X + qs) * kQBytes;
-          mbar_arrive_expect_tx(&bars->q_full[X][qs], w.solo ? kQBytes / 2 : kQBytes);
-          tma_load_4d(qbuf, &tmQ, &bars->q_full[X][qs], 0, 64 * w.j, w.h0, w.b0);
-          if (!w.solo) tma_load_4d(qbuf + kQBytes / 2, &tmQ, &bars->q_full[X][qs], 0, 64 * w.j, w.h1, w.b1);
-        }
-        __syncwarp();
-        ++qk;
-        // K of step s goes out before V of step s-1: V(s-1) waits for PV(s-4), which the MMA
-        // warp issues only with QK(s-1), so K is never held up behind a V slot.
-        const uint32_t bytes = w.solo ? kKBytes : 2 * kKBytes;
-        auto load_pair = [&](const CUtensorMap* map, int bar, uint8_t* buf, int c) {
-          if (elect_one()) {
-            mbar_arrive_expect_tx(&bars->kv_full[X][bar], bytes);
-            tma_load_4d(buf, map, &bars->kv_full[X][bar], 0, 64 * c, w.h0, w.b0);
-            if (!w.solo) tma_load_4d(buf + kKBytes, map, &bars->kv_full[X][bar], 0, 64 * c, w.h1, w.b1);
-          }
-          __syncwarp();
-        };
-        auto load_v = [&](uint32_t s, int c) -> bool {
-          const int vs = s % kPairVStages;
-          if (!warp_mbar_wait(&bars->kv_empty[X][kPairKStages + vs], ((s / kPairVStages) & 1) ^ 1, abort))
-            return false;
-          load_pair(&tmV, kPairKStages + vs, kv0 + (kPairKStages + vs) * kStageBytes, c);
-          return true;
-        };
-        int32_t held = 0;
-        int base = -32, pend_c = -1;
-        for (int i = 0; i < w.n && ok; ++i) {
-          const int32_t e = entry_at(entries, w, i, held, base);
-          if (!(e & fa)) continue;
-          const int c = e & kEntryIdxMask;
-          const int ks = it % kPairKStages;
-          if (!warp_mbar_wait(&bars->kv_empty[X][ks], ((it / kPairKStages) & 1) ^ 1, abort)) { ok = false; break; }
-          load_pair(&tmK, ks, kv0 + ks * kStageBytes, c);
-          if (pend_c >= 0 && !load_v(it - 1, pend_c)) { ok = false; break; }
-          pend_c = c;
-          ++it;
-        }
-        if (ok && pend_c >= 0 && !load_v(it - 1, pend_c)) ok = false;
-      }
-      if (!ok && lane == 0) {
-        fail(abort, 1);
-        for (int s = 0; s < kStages; ++s) {
-          const uint64_t t0 = global_timer_ns();
-          while (!mbar_try_wait(&bars->kv_full[X][s], 0) && !mbar_try_wait(&bars->kv_full[X][s], 1) &&
-                 global_timer_ns() - t0 < 1000000ull) {
-          }
-        }
-      }
-    } else if (warp == 10 || warp == 11) {
-      // ------------------------------------------------------------------ MMA issuers
-      // Per step: one combined wait (both units' K/V slots landed, P of step s-3 written), then
-      // PV(s-3) for both units and QK(s) for both units, as in tc_fwd_kernel.
-      const int X = warp - 10;
-      volatile int* item_slot = item_slots + 2 * X;
-      const uint32_t tcol = tmem + 256 * X;
-      const uint64_t kdesc0 = sw128_desc(smem_u32(smem + kOffKV + X * kStages * kStageBytes), 16, 1024);
-      uint32_t qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
-      bool solo = false;                  // the current item (PVs never cross an item)
-      bool ok = true;
-      // PV of step s (both units) from V stage s % kPairVStages; the caller has waited for P(s),
-      // V(s) and, on an item's first PV, for the epilogue to have read the previous item's O.
-      auto emit_pv = [&](uint32_t s, bool first) {
-        const uint32_t sbuf = s % 3;
-        const int vs = kPairKStages + (int)(s % kPairVStages);
-        if (elect_one()) {
-          const uint64_t va = kdesc0 + (uint64_t)((vs * kStageBytes) >> 4);
-          const uint64_t vb = va + (uint64_t)(kKBytes >> 4);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_bf16_ts(tcol + 192, tcol + 64 * sbuf + 8 * kk, va + (uint64_t)((2048 * kk) >> 4), kIdescPV64,
-                        (first && kk == 0) ? 0u : 1u);
-          if (!solo) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_ts(tcol + 192 + kLane16, tcol + 64 * sbuf + 8 * kk + kLane16,
-                          vb + (uint64_t)((2048 * kk) >> 4), kIdescPV64, (first && kk == 0) ? 0u : 1u);
-          }
-          mma_commit(&bars->o_done[X][s & 1]);
-          mma_commit(&bars->kv_empty[X][vs]);
-        }
-        __syncwarp();
-      };
-      auto issue_pv = [&]() -> bool {
-        const uint32_t s = pvs;
-        if (!warp_mbar_wait2(&bars->p_full[X][s % 3], (s / 3) & 1, &bars->kv_full[X][kPairKStages + s % kPairVStages],
-                             (s / kPairVStages) & 1, true, abort))
-          return false;
-        const bool first = (s == item_first);
-        if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
-        tc_fence_after();
-        emit_pv(s, first);
-        ++pvs;
-        return true;
-      };
-      for (uint32_t k = 0; ok; ++k) {
-        const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
-        const int item = item_slot[slot];
-        __syncwarp();
-        if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
-        __syncwarp();
-        if (item < 0) break;
-        const PItem w = decode_pair(a, rowptr, item);
-        const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
-        int last_used = -1;
-        if (count_steps(entries, w.e0, w.n, fa, last_used) == 0) continue;
-        const int qs = qk % kQSlots;
-        if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
-        ++qk;
-        const uint32_t qaddr = smem_u32(smem + kOffQ + (kQSlots * X + qs) * kQBytes);
-        const uint64_t qda = sw128_desc(qaddr, 16, 1024), qdb = sw128_desc(qaddr + kQBytes / 2, 16, 1024);
-        item_first = steps;
-        solo = w.solo;
-        int32_t held = 0;
-        int base = -32;
-        for (int i = 0; i < w.n && ok; ++i) {
-          const int32_t e = entry_at(entries, w, i, held, base);
-          if (!(e & fa)) continue;
-          const int ks = steps % kPairKStages;
-          while (ok && pvs + kPvLag < steps) ok = issue_pv();
-          if (!ok) break;
-          const bool pv_now = pvs + kPvLag == steps;
-          const uint32_t ps = pvs;
-          const bool pv_first = pv_now && ps == item_first;
-          if (pv_first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) { ok = false; break; }
-          if (!warp_mbar_wait2(&bars->kv_full[X][ks], (steps / kPairKStages) & 1, &bars->p_full[X][ps % 3],
-                               (ps / 3) & 1, pv_now, abort) ||
-              (pv_now && !warp_mbar_wait(&bars->kv_full[X][kPairKStages + ps % kPairVStages],
-                                         (ps / kPairVStages) & 1, abort))) { ok = false; break; }
-          const uint32_t sb = steps % 3;
-          tc_fence_after();
-          if (pv_now) emit_pv(ps, pv_first);
-          if (elect_one()) {
-            const uint64_t ka = kdesc0 + (uint64_t)((ks * kStageBytes) >> 4);
-            const uint64_t kb = ka + (uint64_t)(kKBytes >> 4);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_bf16_ss(tcol + 64 * sb, qda + 2 * kk, ka + 2 * kk, kIdescQK64, kk > 0 ? 1u : 0u);
-            if (!solo) {
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_bf16_ss(tcol + 64 * sb + kLane16, qdb + 2 * kk, kb + 2 * kk, kIdescQK64, kk > 0 ? 1u : 0u);
-            }
-            mma_commit(&bars->s_full[X][sb]);
-            mma_commit(&bars->kv_empty[X][ks]);
-            if (i == last_used) mma_commit(&bars->q_empty[X][qs]);
-          }
-          __syncwarp();
-          if (pv_now) ++pvs;
-          ++steps;
-        }
-        if (!ok) break;
-        while (ok && pvs < steps) ok = issue_pv();
-        if (!ok) break;
-        if (steps > item_first) ++titems;
-      }
-      if (!ok && lane == 0) fail(abort, 3);
-      if (elect_one()) mma_commit(&bars->drain);
-      __syncwarp();
-      if (lane == 0) {
-        const uint64_t t0 = global_timer_ns();
-        while (!mbar_try_wait(&bars->drain, 0) && global_timer_ns() - t0 < kWaitLimitNs) {
-        }
-      }
-      __syncwarp();
-    } else {
-      // ------------------------------------------------------------------ softmax + epilogue
-      const int X = warp >> 2;                 // tile worker
-      const bool upper = lane >= 16;           // partner unit's lanes
-      const int r64 = 16 * (warp & 3) + (lane & 15);   // query row within chunk j
-      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-      const uint32_t tcol = tmem + 256 * X;
-      volatile int* item_slot = item_slots + 2 * X;
-      uint64_t* s_full = bars->s_full[X];
-      uint64_t* p_full = bars->p_full[X];
-      uint64_t* o_done = bars->o_done[X];
-      uint64_t* o_free = &bars->o_free[X];
-      uint32_t it = 0, sb_c = 0, ph_c = 0;
-      bool s_ready = false;
-      bool ok = true;
-      for (uint32_t k = 0; ok; ++k) {
-        const int slot = k & 1;
-        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
-        const int item = item_slot[slot];
-        mbar_arrive(&bars->item_empty[X][slot]);
-        if (item < 0) break;
-        const PItem w = decode_pair(a, rowptr, item);
-        const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
-        const int32_t fd = (w.j & 1) ? kFlagDiag1 : kFlagDiag0;
-        const bool live = !(w.solo && upper);
-        float m = -INFINITY, l = 0.f;
-        int nsteps = 0;
-        for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
-          const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
-          uint32_t own = __ballot_sync(0xffffffffu, (eb & fa) != 0);
-          while (own) {
-            const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
-            own &= own - 1;
-            ++nsteps;
-            const uint32_t sb = sb_c;
-            if (!s_ready && !warp_mbar_wait(&s_full[sb], ph_c, abort)) { ok = false; break; }
-            tc_fence_after();
-            uint32_t sr[64];
-            XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb, sr);
-            XSAKE_TMEM_LD32(tcol + lane_base + 64 * sb + 32, (sr + 32));
-            const bool next_done = mbar_test_wait(&s_full[sb_c == 2 ? 0 : sb_c + 1], sb_c == 2 ? ph_c ^ 1u : ph_c);
-            XSAKE_TMEM_WAIT_LD32(sr);
-            XSAKE_TMEM_WAIT_LD32((sr + 32));
-            s_ready = __all_sync(0xffffffffu, next_done);
-            uint32_t pk[32];
-            float* x = reinterpret_cast<float*>(sr);   // raw scores
-            // Keys past the token-level causal cut on the diagonal chunk, and every key of a
-            // lane whose unit is absent (a lone unit), are masked.
-            const int lim = !live ? -1 : ((e & fd) ? r64 : 63);
-            if (__any_sync(0xffffffffu, lim < 63)) {
-#pragma unroll
-              for (int j = 0; j < 64; ++j)
-                if (j > lim) x[j] = -INFINITY;
-            }
-            float t1[22];
-#pragma unroll
-            for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
-            t1[21] = x[63];
-            float t2[8];
-#pragma unroll
-            for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
-            t2[7] = t1[21];
-            const float mraw =
-                fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
-            const float mx = mraw * p.scale_log2;
-            const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
-            if (m == -INFINITY) m = mx;
-            if (__any_sync(0xffffffffu, need)) {
-              if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
-              tc_fence_after();
-              const float alpha = need ? ex2(m - mx) : 1.0f;
-              uint32_t orow[32];
-#pragma unroll
-              for (int hcol = 0; hcol < 2; ++hcol) {
-                XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
-                XSAKE_TMEM_WAIT_LD32(orow);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) orow[j] = __float_as_uint(__uint_as_float(orow[j]) * alpha);
-                XSAKE_TMEM_ST32(tcol + lane_base + 192 + 32 * hcol, orow);
-              }
-              tmem_wait_st();
-              if (need) {
-                l *= alpha;
-                m = mx;
-              }
-            }
-            const float msub = (m == -INFINITY) ? 0.f : m;
-            const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nm = pk2(-msub, -msub);
-            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float x0, x1, p0, p1;
-              upk2(fma2(pk2(x[2 * j], x[2 * j + 1]), cc, nm), x0, x1);
-              if ((j & 7) < 2) {
-                exp2_poly2(x0, x1, p0, p1);
-              } else {
-                p0 = ex2(x0);
-                p1 = ex2(x1);
-              }
-              acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
-              __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-              pk[j] = *reinterpret_cast<uint32_t*>(&pb);
-            }
-            float s0, s1;
-            upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
-            l += s0 + s1;
-            XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
-            tmem_wait_st();
-            tc_fence_before();
-            mbar_arrive(&p_full[sb]);
-            ++it;
-            if (++sb_c == 3) {
-              sb_c = 0;
-              ph_c ^= 1;
-            }
-          }
-        }
-        if (!ok) break;
-        // ---------------------------------------------------------------- epilogue
-        const int bb = upper ? w.b1 : w.b0, hh = upper ? w.h1 : w.h0;
-        const int tok = 64 * w.j + r64;
-        const bool valid = live && tok < a.S;
-        const bool empty = valid && !(l > 0.f);
-        uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + bb * a.os[0] +
-                                                 hh * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
-        if (nsteps > 0) {
-          // The same two-phase wait for the last PVs as in tc_fwd_kernel.
-          if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
-          if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
-          tc_fence_after();
-          const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-          for (int hcol = 0; hcol < 2; ++hcol) {
-            uint32_t orow[32];
-            XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
-            XSAKE_TMEM_WAIT_LD32(orow);
-            if (valid && !empty) {
-#pragma unroll
-              for (int cc = 0; cc < 4; ++cc) {
-                uint32_t wv[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  __nv_bfloat162 pb = __floats2bfloat162_rn(__uint_as_float(orow[8 * cc + 2 * q]) * inv,
-                                                            __uint_as_float(orow[8 * cc + 2 * q + 1]) * inv);
-                  wv[q] = *reinterpret_cast<uint32_t*>(&pb);
-                }
-                orow_g[4 * hcol + cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-              }
-            }
-          }
-          tc_fence_before();
-          mbar_arrive(o_free);
-        }
-        const bool empty_lo = __any_sync(0xffffffffu, empty && !upper);
-        const bool empty_hi = __any_sync(0xffffffffu, empty && upper);
-        if (empty_lo || empty_hi) {
-          // Rows with no live score attend uniformly (the reference's finfo.min fill).
-          float2 mean0 = make_float2(0.f, 0.f), mean1 = make_float2(0.f, 0.f);
-          if (empty_lo) warp_mean_v(a, w.b0, w.h0, mean0);
-          if (empty_hi) warp_mean_v(a, w.b1, w.h1, mean1);
-#pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
-            uint32_t wv[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int src = 4 * cc + q;
-              const float x0 = __shfl_sync(0xffffffffu, mean0.x, src), y0 = __shfl_sync(0xffffffffu, mean0.y, src);
-              const float x1 = __shfl_sync(0xffffffffu, mean1.x, src), y1 = __shfl_sync(0xffffffffu, mean1.y, src);
-              __nv_bfloat162 pb = __floats2bfloat162_rn(upper ? x1 : x0, upper ? y1 : y0);
-              wv[q] = *reinterpret_cast<uint32_t*>(&pb);
-            }
-            if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-          }
-        }
-        if (valid) a.lse[(int64_t)(bb * a.H + hh) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
-      }
-      if (!ok) fail(abort, 4);
-    }
+    const FwdCtx c{smem, bars, abort, item_slots, tmem, a.plan + L.f_rowptr_off, a.plan + L.f_entries_off};
+    // The plan compiler chose the pairing from the mask (H_FWD_PAIR); every CTA reads the same word.
+    if (a.plan[H_FWD_PAIR])
+      pair_roles(tmQ, tmK, tmV, p, c);
+    else
+      tile_roles(tmQ, tmK, tmV, p, c);
   }
 
   tc_fence_before();
@@ -1105,8 +1091,6 @@ tc_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 constexpr int kMaxDev = 64;
 std::once_flag g_attr_once[kMaxDev];
 cudaError_t g_attr_err[kMaxDev];
-std::once_flag g_pair_attr_once[kMaxDev];
-cudaError_t g_pair_attr_err[kMaxDev];
 
 }  // namespace
 
@@ -1178,39 +1162,26 @@ int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
                 di.minor);
   XSAKE_REQUIRE(ws != nullptr && ws_bytes >= 256 && ((uintptr_t)ws & 15) == 0, XSAKE_EINVAL,
                 "the tensor-core forward needs a 256-byte, 16-byte aligned workspace (got %zu bytes)", ws_bytes);
-  // Units that share a mask are paired (tc_fwd_pair_kernel) whenever there are two of them;
-  // a mask per unit leaves only the query-chunk pairing of tc_fwd_kernel.
-  const bool paired = pair_units(a.L, a.B, a.H) >= 2;
+  // The plan (H_FWD_PAIR) chooses the pairing on the device; the grid covers either item count.
   CUtensorMap mq, mk, mv;
-  if ((st = tc_make_map(&mq, a.q, a.qs, a.B, a.H, a.S, paired ? 64 : 128))) return st;
+  if ((st = tc_make_map(&mq, a.q, a.qs, a.B, a.H, a.S, 64))) return st;
   if ((st = tc_make_map(&mk, a.k, a.ks, a.B, a.H, a.S, 64))) return st;
   if ((st = tc_make_map(&mv, a.v, a.vs, a.B, a.H, a.S, 64))) return st;
   int dev = 0;
   XSAKE_CUDA_TRY(cudaGetDevice(&dev));
   XSAKE_REQUIRE(dev < kMaxDev, XSAKE_EUNSUPPORTED, "device ordinal %d", dev);
-  TcParams p;
-  p.a = a;
-  p.scale_log2 = a.scale * kLog2e;
-  p.counter = reinterpret_cast<int*>(ws);
-  if (paired) {
-    std::call_once(g_pair_attr_once[dev], [dev] {
-      g_pair_attr_err[dev] =
-          cudaFuncSetAttribute(tc_fwd_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    });
-    XSAKE_REQUIRE(g_pair_attr_err[dev] == cudaSuccess, XSAKE_ECUDA, "cudaFuncSetAttribute: %s",
-                  cudaGetErrorString(g_pair_attr_err[dev]));
-    XSAKE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(int), s));
-    const int grid = std::max(1, std::min((pair_items(a.L, a.B, a.H) + 1) / 2, di.sm_count));
-    tc_fwd_pair_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
-    return check_launch("tc_fwd_pair_kernel");
-  }
   std::call_once(g_attr_once[dev], [dev] {
     g_attr_err[dev] = cudaFuncSetAttribute(tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   });
   XSAKE_REQUIRE(g_attr_err[dev] == cudaSuccess, XSAKE_ECUDA, "cudaFuncSetAttribute: %s",
                 cudaGetErrorString(g_attr_err[dev]));
+  TcParams p;
+  p.a = a;
+  p.scale_log2 = a.scale * kLog2e;
+  p.counter = reinterpret_cast<int*>(ws);
   XSAKE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(int), s));
-  const int grid = std::max(1, std::min((a.L.nitems + 1) / 2, di.sm_count));
+  const int items = std::max(a.L.nitems, pair_items(a.L, a.B, a.H));
+  const int grid = std::max(1, std::min((items + 1) / 2, di.sm_count));
   tc_fwd_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
   return check_launch("tc_fwd_kernel");
 }

@@ -1,7 +1,7 @@
 // Compiled block-mask plan: layout shared by the plan compiler and the attention kernels.
 //
 // A plan is one caller-owned device buffer of int32 words:
-//   header    kPlanHeaderWords words (magic, dims, device-written counts)
+//   header    kPlanHeaderWords words (magic, dims, device-written counts, forward pairing)
 //   mask      raw uint8 mask [Bm, Hm, nq, nk] (copy of the caller's mask)
 //   qempty    uint8 [Bm, Hm, nq]: 1 when every token of the q-block is fully masked
 //   -- built only when block_size % 64 == 0 and S % 64 == 0 (the tensor-core path) --
@@ -19,7 +19,7 @@
 namespace xsake {
 
 constexpr int32_t kPlanMagic = 0x504B5358;  // "XSKP"
-constexpr int32_t kPlanVersion = 2;
+constexpr int32_t kPlanVersion = 3;
 constexpr int kPlanHeaderWords = 32;
 
 // Entry encoding: low 20 bits = chunk index, then flags.
@@ -36,6 +36,7 @@ enum PlanHeader : int {
   H_F_NNZ, H_B_NNZ,
   H_ACTIVE_LO = 16, H_ACTIVE_HI, H_TILES_LO, H_TILES_HI, H_EMPTY_LO, H_EMPTY_HI,
   H_ITEMS_LO, H_ITEMS_HI,
+  H_FWD_PAIR,   // 1: the forward pairs units that share a mask (see attn_fwd_tc.cu), 0: query chunks
 };
 
 struct PlanLayout {
