@@ -627,6 +627,10 @@ __device__ __forceinline__ int count_steps(const int32_t* entries, int e0, int n
 constexpr uint32_t kIdescQK64 = idesc_bf16(64, 64, false);
 constexpr uint32_t kIdescPV64 = idesc_bf16(64, 64, true);
 constexpr uint32_t kLane16 = 16u << 16;   // TMEM address of the partner unit's lanes
+// PV lag of the unit pairing: 2 measured 1% faster than 3 there (one step less QK run-ahead,
+// PV issued a step sooner); the query-chunk pairing keeps 3 (2 was 3% slower on a dense mask).
+// QK(s) still follows PV(s-3) in issue order, so the S buffer it overwrites has been read.
+constexpr uint32_t kPairPvLag = 2;
 constexpr int kPairKStages = 2;           // K ring (both units' K chunks per stage), released by QK
 constexpr int kPairVStages = 3;           // V ring, released by PV
 static_assert(kPairKStages + kPairVStages <= kStages, "the pair rings reuse the K/V ring's shared memory");
@@ -792,9 +796,9 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
         const int32_t e = entry_at(entries, w, i, held, base);
         if (!(e & fa)) continue;
         const int ks = steps % kPairKStages;
-        while (ok && pvs + kPvLag < steps) ok = issue_pv();
+        while (ok && pvs + kPairPvLag < steps) ok = issue_pv();
         if (!ok) break;
-        const bool pv_now = pvs + kPvLag == steps;
+        const bool pv_now = pvs + kPairPvLag == steps;
         const uint32_t ps = pvs;
         const bool pv_first = pv_now && ps == item_first;
         if (pv_first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) { ok = false; break; }
