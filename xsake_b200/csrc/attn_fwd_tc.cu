@@ -9,8 +9,9 @@
 // returned.
 //
 // Each CTA (one per SM, persistent) runs two independent tile workers that share only the SM:
-// each takes its own work items (128 query rows = 64-row chunks 2t, 2t+1 of one (b, h)) from a
-// global counter, longest first, and walks the ascending list of 64-key chunks the tile attends
+// each takes its own work items (128 query rows: in the query-chunk pairing the 64-row chunks
+// 2t, 2t+1 of one (b, h), in the unit pairing one chunk of two units) from a global counter,
+// longest first, and walks the ascending list of 64-key chunks the tile attends
 // through its own 5-stage K/V ring (TMA, SWIZZLE_128B).  Two workers rather than one 256-row
 // item over a merged chunk list: a merged walk made each tile's MMA warp wait on and release the
 // other tile's chunks and kept the two softmax groups in lock-step (their exponential phases
