@@ -505,7 +505,21 @@ __global__ void __launch_bounds__(256) xent_fwd_kernel(const T* __restrict__ log
     int64_t c0 = 0;
     if (VEC) {
       const int64_t nv = vocab / N;
-      for (int64_t vi = lane; vi < nv; vi += 32) {
+      // Four 16-byte loads a lane in flight per round (the rows are ~100 KB: the loop is bound by
+      // memory-level parallelism, not arithmetic).
+      int64_t vi = lane;
+      for (; vi + 96 < nv; vi += 128) {
+        uint4 raw[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) raw[u] = *reinterpret_cast<const uint4*>(r + (vi + 32 * u) * N);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float v[N];
+          Vec<T>::from_raw(raw[u], v);
+          add(v, N);
+        }
+      }
+      for (; vi < nv; vi += 32) {
         float v[N];
         Vec<T>::load(r + vi * N, v);
         add(v, N);
@@ -561,7 +575,23 @@ __global__ void __launch_bounds__(256) xent_bwd_kernel(const T* __restrict__ log
     int64_t c0 = 0;
     if (VEC) {
       const int64_t nv = ld / N;   // whole rows of vectors: ld % N == 0
-      for (int64_t vi = lane; vi < nv; vi += 32) {
+      const int64_t nfull = vocab / N;   // vectors entirely inside the vocabulary
+      int64_t vi = lane;
+      // Four 16-byte loads a lane in flight per round over the vectors inside the vocabulary.
+      for (; vi + 96 < nfull; vi += 128) {
+        uint4 raw[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) raw[u] = *reinterpret_cast<const uint4*>(r + (vi + 32 * u) * N);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          float v[N], o[N];
+          Vec<T>::from_raw(raw[u], v);
+#pragma unroll
+          for (int i = 0; i < N; ++i) o[i] = g_of((vi + 32 * u) * N + i, v[i]);
+          Vec<T>::store(gr + (vi + 32 * u) * N, o);
+        }
+      }
+      for (; vi < nv; vi += 32) {
         float v[N], o[N];
         if ((vi + 1) * N <= vocab) {
           Vec<T>::load(r + vi * N, v);
