@@ -1,13 +1,16 @@
 #!/usr/bin/env python
 """Benchmark of the HADS block-sparse attention forward on B200.
 
-Default workload (one "step" = one forward over one batch):
+Default workload (one "step" = one forward over the whole job):
   bf16 B=4 H=12 S=4096 D=64, 64x64 blocks, HADS masks from dummy_hads_profile (the profile the
-  reference's own attention benchmark uses) with causal cut and global KV block 0, per rank.
+  reference's own attention benchmark uses) with causal cut and global KV block 0.
 Metric: effective TFLOP/s over active blocks, 4*D*64*64 FLOPs per active (q-block, kv-block)
-pair after the causal cut (n_a), whole job (all ranks).  Multi-GPU: one process per GPU, each
-rank runs its own batch of 4 (weak scaling), no collective on the data path; timing is the max
-over ranks of CUDA-event time.
+pair after the causal cut (n_a), whole job.  Multi-GPU (strong scaling): every rank holds the
+same job and computes its share of the 48 (batch, head) units (assigned two batch units of a
+head at a time, longest first); no collective on the data path; the time is the max over ranks
+of CUDA-event time.  The weak-scaling number (every rank runs the whole job) is a secondary
+field, as are the backward, the row kernels and the calibration exchange, each split over the
+ranks the same way.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl xsake|reference]
                     [--workload attn|attn_bwd|calib|train|softmax|layernorm|entropy]
@@ -20,6 +23,7 @@ of the same workload on the host cores, rank 0 only.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import math
 import os
@@ -35,7 +39,9 @@ sys.path.insert(0, ROOT)
 
 B, H, S, D, BS = 4, 12, 4096, 64, 64
 FLOP_PER_BLOCK = 4 * D * 64 * 64          # QK^T + PV of one 64x64 active tile
+BWD_FLOP_PER_BLOCK = 10 * D * 64 * 64     # S, dP, dV, dK, dQ
 L2_BYTES = 126 * 2 ** 20
+METRIC = "HADS attn fwd active-block TFLOP/s (bf16 B=4 H=12 S=4096 D=64)"
 
 
 def _peaks():
@@ -123,25 +129,27 @@ def _barrier(dist):
         dist.barrier()
 
 
-def _max_over_ranks(x: float, dist):
+def _reduce(x: float, dist, op: str):
     if dist is None:
         return x
     import torch
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return float(t.item())
 
 
-def _sum_over_ranks(x: float, dist):
+def _gather(vals, dist, world):
+    """All ranks' float vectors (same length) as a list per rank."""
     if dist is None:
-        return x
+        return [list(vals)]
     import torch
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [x.cpu().tolist() for x in out]
 
 
-# ----------------------------------------------------------------------------- masks / inputs
+# ----------------------------------------------------------------------------- masks / job
 def hads_masks():
     from xsake_b200 import hads_pattern as hp
     prof = hp.dummy_hads_profile(H, S, BS, causal=True, global_blocks=1)
@@ -152,27 +160,37 @@ def n_active(masks, batch):
     return int(np.tril(masks).sum()) * batch
 
 
-# ----------------------------------------------------------------------------- reference arm
-_TMASK = {}
+def job_config(masks):
+    """The workload (the same dict in both arms)."""
+    na = n_active(masks, B)
+    return {"workload": "hads_attn_fwd_bf16_B4_H12_S4096_D64_block64", "batch": B, "heads": H, "seq_len": S,
+            "head_dim": D, "block": BS, "mask": "dummy_hads_profile rho 0.1-0.9, window 2, causal, global block 0",
+            "active_blocks": na, "flops_per_step": na * FLOP_PER_BLOCK}
 
 
+def shards(masks, world):
+    from xsake_b200 import calibration as cal
+    return cal.pair_shard(masks, B, world)
+
+
+# ----------------------------------------------------------------------------- CPU reference
 def cpu_reference_step(q, k, v, masks, h, t):
-    """One step of the reference CPU path (sparse_attention_reference: dense scores, token mask,
+    """One step of the reference CPU path (sparse_attention_reference: token mask from the block
+    mask (repeat + tril, built per call as the reference does), dense scores, finfo.min fill,
     softmax, P.V) for the 128 query rows [128t, 128t+128) of head h against all S keys, float32
-    NumPy (oracle port).  Returns the active-block FLOPs of those rows."""
+    NumPy (oracle port).  Its cost does not depend on the mask."""
     from oracle import attention as oa
-    tm = _TMASK.get(h)
-    if tm is None:
-        tm = _TMASK[h] = oa.token_mask(masks[h], BS, S, True)
     rows = slice(128 * t, 128 * t + 128)
-    oa._slice_forward(q[0, h, rows], k[0, h], v[0, h], tm[rows], D ** -0.5, np.float32)
-    return int(np.tril(masks[h])[2 * t:2 * t + 2].sum()) * FLOP_PER_BLOCK
+    tm = np.repeat(np.repeat(masks[h][2 * t:2 * t + 2], BS, axis=0), BS, axis=1)
+    tm &= np.arange(S)[None, :] <= (128 * t + np.arange(128))[:, None]
+    oa._slice_forward(q[0, h, rows], k[0, h], v[0, h], tm, D ** -0.5, np.float32)
 
 
-def _ref_schedule(i):
-    """(head, 128-row tile) of reference step i: heads cycle fastest, tiles advance by a stride
-    coprime with S/128 so short runs still sample early and late (short and long) rows."""
-    return i % H, (7 * (i // H) + 3) % (S // 128)
+def _ref_schedule(n):
+    """(head, 128-row tile) of the first n reference steps: a fixed pseudo-random order of all
+    H x S/128 tiles (every tile costs the same dense work)."""
+    order = np.random.default_rng(5).permutation(H * (S // 128))
+    return [(int(i) // (S // 128), int(i) % (S // 128)) for i in order[np.arange(n) % len(order)]]
 
 
 def cpu_inputs():
@@ -181,19 +199,53 @@ def cpu_inputs():
     return oi.to_bf16(q).astype(np.float32), oi.to_bf16(k).astype(np.float32), oi.to_bf16(v).astype(np.float32)
 
 
-def cpu_baseline(masks, budget_s=10.0):
+def _cpu_desc():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max((x.get("num_threads", 1) for x in threadpool_info()), default=1)
+    except Exception:   # noqa: BLE001 - informational only
+        return os.cpu_count()
+
+
+def cpu_tiles(masks, n=None, budget_s=None):
+    """Times reference steps; credits each with the job's mean active-block FLOPs per tile, so
+    the value is the whole job's active-block FLOPs over the time the reference path would take
+    for all H * S/128 tiles of one batch unit (an unbiased estimate whatever tiles are drawn).
+    Returns (TFLOP/s, tiles, seconds)."""
     q, k, v = cpu_inputs()
+    flops_per_tile = n_active(masks, 1) * FLOP_PER_BLOCK / (H * (S // 128))
     cpu_reference_step(q, k, v, masks, 0, 0)
-    flops, n, t0 = 0, 0, time.perf_counter()
-    while True:
-        flops += cpu_reference_step(q, k, v, masks, *_ref_schedule(n))
-        n += 1
-        if time.perf_counter() - t0 > budget_s:
+    sched = _ref_schedule(n if n is not None else 100000)
+    t0 = time.perf_counter()
+    done = 0
+    for h, t in sched:
+        cpu_reference_step(q, k, v, masks, h, t)
+        done += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n} tiles of 128 query rows x all 4096 keys of the bf16 B=4 H=12 S=4096 D=64 "
-                      f"workload (dense float32 NumPy port of sparse_attention_reference), {dt:.1f} s"}
+    return flops_per_tile * done / dt / 1e12, done, dt
+
+
+def cpu_baseline(masks, budget_s=10.0):
+    value, n, dt = cpu_tiles(masks, budget_s=budget_s)
+    return {"value": value, "unit": "TFLOP/s", "cores": _blas_threads(), "kind": "port",
+            "host": f"{os.cpu_count()} cores, {_cpu_desc()}",
+            "sample": f"{n} tiles of 128 query rows x all 4096 keys drawn in a fixed random order from the "
+                      f"{H * S // 128} tiles of one batch unit of the workload (dense float32 NumPy port of "
+                      f"sparse_attention_reference), {dt:.1f} s; each tile credited with the job's mean "
+                      "active-block FLOPs per tile"}
 
 
 def run_reference(args):
@@ -202,30 +254,68 @@ def run_reference(args):
         return
     masks = hads_masks()
     q, k, v = cpu_inputs()
-    for i in range(args.warmup):
-        cpu_reference_step(q, k, v, masks, *_ref_schedule(i))
-    flops, t0 = 0, time.perf_counter()
-    for i in range(args.steps):
-        flops += cpu_reference_step(q, k, v, masks, *_ref_schedule(i))
+    sched = _ref_schedule(args.warmup + args.steps)
+    for h, t in sched[:args.warmup]:
+        cpu_reference_step(q, k, v, masks, h, t)
+    flops_per_tile = n_active(masks, 1) * FLOP_PER_BLOCK / (H * (S // 128))
+    t0 = time.perf_counter()
+    for h, t in sched[args.warmup:]:
+        cpu_reference_step(q, k, v, masks, h, t)
     dt = time.perf_counter() - t0
-    value = flops / dt / 1e12
-    line = {"metric": "HADS attn fwd active-block TFLOP/s (bf16 B=4 H=12 S=4096 D=64)", "value": value,
-            "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "hads_attn_fwd_bf16_B4_H12_S4096_D64_block64", "batch_per_rank": B,
-                       "heads": H, "seq_len": S, "head_dim": D, "block": BS,
-                       "mask": "dummy_hads_profile rho 0.1-0.9, window 2, causal, global block 0",
-                       "active_blocks_per_rank": n_active(masks, B),
-                       "flops_per_step_per_rank": n_active(masks, B) * FLOP_PER_BLOCK,
-                       "parallelism": "reference CPU path on the host cores of rank 0",
-                       "step": "128 query rows x 4096 keys of one head, dense float32 (reference CPU path); "
-                               "value counts the active-block FLOPs of those rows"},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": f"{args.steps} tiles of 128 query rows x 4096 keys, dense float32 "
-                                       "NumPy port of sparse_attention_reference"},
+    value = flops_per_tile * args.steps / dt / 1e12
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": job_config(masks),
+            "parallelism": f"reference CPU path on the host cores of rank 0 ({os.cpu_count()} cores, {_cpu_desc()})",
+            "step": "128 query rows x 4096 keys of one head (dense float32, the reference CPU path), credited "
+                    "with the job's mean active-block FLOPs per tile",
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": _blas_threads(), "kind": "port",
+                             "sample": f"{args.steps} tiles of 128 query rows x 4096 keys in a fixed random order "
+                                       "over all tiles, dense float32 NumPy port of sparse_attention_reference"},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- timing helpers
+def _time_calls(fn, n, dist, warmup=3):
+    """Mean ms per call of fn() (CUDA events on the current stream), max over ranks."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    _barrier(dist)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return _reduce(e0.elapsed_time(e1) / n, dist, "max")
+
+
+def _graph_calls(calls, dist, reps=10, per_graph=20):
+    """ms per call of the given C-ABI calls replayed as a CUDA graph of `per_graph` calls (launch
+    latency amortised), max over ranks."""
+    import torch
+    from xsake_b200 import _lib
+
+    def run_all():
+        for i in range(per_graph):
+            st = calls[i % len(calls)]()
+            if st:
+                _lib.check(st)
+    run_all()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run_all()
+    return _time_calls(g.replay, reps, dist) / per_graph
+
+
+def _split_rows(n, world, rank):
+    lo = n * rank // world
+    return lo, n * (rank + 1) // world
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -233,36 +323,38 @@ def run_attention(args, dist, rank, world, local):
     import ctypes as C
     import torch
     from xsake_b200 import _lib, sparse_attention as sa
-    from xsake_b200 import _device as dev
 
     masks = hads_masks()
-    cm = sa.compile_block_mask(masks, B, H, S, BS, True)
+    cfg = job_config(masks)
+    my_units = shards(masks, world)[rank]
+    cm = sa.compile_block_mask(masks, B, H, S, BS, True, units=my_units)
+    cm_full = sa.compile_block_mask(masks, B, H, S, BS, True)
+    st = cm.stats()
+    na_rank = st["active_blocks"]
     set_bytes = 4 * B * H * S * D * 2
     nsets = max(2, math.ceil(3 * L2_BYTES / set_bytes) + 1)
-    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    g = torch.Generator(device="cuda").manual_seed(1003)          # the same job on every rank
     sets = []
     tau = torch.linspace(0.25, 4.0, H, device="cuda").view(1, H, 1, 1)
     for _ in range(nsets):
         q = (torch.randn(B, H, S, D, device="cuda", generator=g) * tau).to(torch.bfloat16)
         k = torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16)
         v = torch.randn(B, H, S, D, device="cuda", generator=g).to(torch.bfloat16)
-        o = torch.empty_like(q)
-        lse = torch.empty(B, H, S, device="cuda")
-        sets.append((q, k, v, o, lse))
+        sets.append((q, k, v, torch.empty_like(q), torch.empty(B, H, S, device="cuda")))
     lib = _lib.load()
     desc = sa._desc(sets[0][0], sets[0][1], sets[0][2], sets[0][3], cm, None)
     ws_n = C.c_size_t(0)
     _lib.check(lib.xsake_attn_fwd_workspace_size(C.byref(desc), C.byref(ws_n)))
-    ws = torch.empty(max(ws_n.value, 16), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(max(ws_n.value, 256), dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     sp = stream.cuda_stream
 
-    def step(i):
+    def step(i, plan=cm):
         q, k, v, o, lse = sets[i % nsets]
-        st = lib.xsake_attn_fwd(C.byref(desc), cm.plan.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                o.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), sp)
-        if st:
-            _lib.check(st)
+        r = lib.xsake_attn_fwd(C.byref(desc), plan.plan.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                               o.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), sp)
+        if r:
+            _lib.check(r)
 
     step(0)
     torch.cuda.synchronize()
@@ -287,28 +379,35 @@ def run_attention(args, dist, rank, world, local):
     total_ms = e0.elapsed_time(e1)
     kernel_ms = float(np.mean([ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(args.steps)]))
     assert _lib.device_error(sp) == 0
-    total_ms_max = _max_over_ranks(total_ms, dist)
-
-    na = n_active(masks, B)
-    flops_rank = na * FLOP_PER_BLOCK
-    value = world * flops_rank * args.steps / (total_ms_max * 1e-3) / 1e12
+    per_rank = _gather([float(len(my_units)), float(na_rank), kernel_ms, total_ms / args.steps,
+                        float(st["split_items"]), float(st["work_items"])], dist, world)
+    total_ms_max = max(r[3] for r in per_rank) * args.steps
+    slow = max(range(world), key=lambda r: per_rank[r][3])
+    value = cfg["flops_per_step"] * args.steps / (total_ms_max * 1e-3) / 1e12
     peak_tf, _, peak_kind = _peaks()
-    achieved = flops_rank / (kernel_ms * 1e-3) / 1e12
+    achieved = per_rank[slow][1] * FLOP_PER_BLOCK / (per_rank[slow][2] * 1e-3) / 1e12
 
-    # End to end through the public API: pinned host q/k/v -> GPU -> attention -> pinned host
-    # out, every step.  Steps alternate between two streams, as a serving loop would issue them,
-    # so the upload of step i+1 overlaps the download of step i (the copies are PCIe-bound; the
-    # kernel is ~7% of a step).
+    # Weak scaling (secondary): every rank runs the whole job.
+    weak = None
+    if world > 1:
+        full_ms = _time_calls(lambda it=iter(range(10 ** 9)): step(next(it), cm_full), args.steps, dist)
+        weak = {"value": world * cfg["flops_per_step"] / (full_ms * 1e-3) / 1e12, "ms_per_step": full_ms,
+                "unit": "TFLOP/s", "note": "every rank runs the whole B=4 job (replicas, no collective)"}
+
+    # End to end through the public API: pinned host q/k/v -> GPU (this rank's units' slices) ->
+    # attention -> pinned host out (those slices), every step.  Steps alternate between two
+    # streams, as a serving loop issues independent batches, so one step's upload overlaps the
+    # previous step's download.
     e2e_steps = max(3, min(args.steps, 50))
     hq, hk, hv = (t.cpu().pin_memory() for t in sets[0][:3])
     houts = [torch.empty_like(hq).pin_memory() for _ in range(2)]
     e2e_streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    bufs = [tuple(torch.empty_like(sets[0][0]) for _ in range(4)) for _ in range(2)]
 
     def e2e_step(i):
         with torch.cuda.stream(e2e_streams[i % 2]):
-            out = sa.sparse_attention_pallas(hq.cuda(non_blocking=True), hk.cuda(non_blocking=True),
-                                             hv.cuda(non_blocking=True), masks, BS, BS, None, True)
-            houts[i % 2].copy_(out, non_blocking=True)
+            sa.sparse_attention_shard(hq, hk, hv, masks, my_units, BS, None, True, out=houts[i % 2],
+                                      buffers=bufs[i % 2])
 
     for i in range(4):
         e2e_step(i)
@@ -325,36 +424,177 @@ def run_attention(args, dist, rank, world, local):
     a1.record(stream)
     torch.cuda.synchronize()
     _barrier(dist)
-    e2e_ms = _max_over_ranks(a0.elapsed_time(a1), dist)
-    e2e_value = world * flops_rank * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    e2e_ms = _reduce(a0.elapsed_time(a1), dist, "max")
+    e2e_value = cfg["flops_per_step"] * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    unit_bytes = S * D * 2
+
+    secondary = None if args.no_secondary else run_secondary(args, dist, rank, world, masks, my_units, sets, cm)
 
     cpu = cpu_baseline(masks) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
-    st = cm.stats()
     if rank == 0:
         line = {
-            "metric": "HADS attn fwd active-block TFLOP/s (bf16 B=4 H=12 S=4096 D=64)",
-            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": total_ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "hads_attn_fwd_bf16_B4_H12_S4096_D64_block64", "batch_per_rank": B,
-                       "heads": H, "seq_len": S, "head_dim": D, "block": BS,
-                       "mask": "dummy_hads_profile rho 0.1-0.9, window 2, causal, global block 0",
-                       "active_blocks_per_rank": na, "computed_tiles_per_rank": st["computed_tiles"],
-                       "flops_per_step_per_rank": flops_rank,
-                       "l2": f"{nsets} rotating input sets of {set_bytes / 1e6:.0f} MB (> 126 MB L2)",
-                       "parallelism": f"weak, {world} rank(s) x batch {B}, no collective"},
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": cfg,
+            "parallelism": f"batch x heads of the one job split over {world} rank(s) "
+                           "(unit pairs of a head, longest first), no collective",
+            "l2": f"{nsets} rotating input sets of {set_bytes / 1e6:.0f} MB (> 126 MB L2)",
+            "ranks": [{"rank": r, "units": int(x[0]), "active_blocks": int(x[1]), "kernel_ms": x[2],
+                       "ms_per_step": x[3], "split_items": int(x[4]), "work_items": int(x[5])}
+                      for r, x in enumerate(per_rank)],
+            "plan": {"pairing": st["pairing"], "computed_tiles_rank0": st["computed_tiles"],
+                     "split_cap": st["split_cap"], "workers": st["workers"]},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "peak_source": f"bf16_tflops ({peak_kind}, burst)",
-                         "kernel": "tc_fwd_kernel (unit pairing)", "kernel_ms": kernel_ms, "traffic": _traffic("attn")},
+                         "kernel": f"tc_fwd_kernel ({st['pairing']} pairing) of the slowest rank ({slow})",
+                         "kernel_ms": per_rank[slow][2], "traffic": _traffic("attn") if world == 1 else None},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": 3 * B * H * S * D * 2, "d2h_bytes_per_step": B * H * S * D * 2,
-                    "steps": e2e_steps, "api": "xsake_b200.sparse_attention.sparse_attention_pallas",
-                    "streams": 2},
+                    "h2d_bytes_per_step": 3 * B * H * unit_bytes, "d2h_bytes_per_step": B * H * unit_bytes,
+                    "steps": e2e_steps, "api": "xsake_b200.sparse_attention.sparse_attention_shard",
+                    "streams": 2, "per_rank": "each rank copies its own units' [S, D] slices"},
+            "weak_scaling": weak,
+            "secondary": secondary,
             "gpu_launches": args.steps,
             "clocks": ck,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
+
+
+def run_secondary(args, dist, rank, world, masks, my_units, sets, cm):
+    """The other hot-path kernels, split over the ranks like the headline, max over ranks."""
+    import ctypes as C
+    import torch
+    from xsake_b200 import _lib, comm as xcomm, hads_pattern as hp, sparse_attention as sa
+    lib = _lib.load()
+    sp = lambda: torch.cuda.current_stream().cuda_stream   # noqa: E731
+    _, hbm, kind = _peaks()
+    peak_tf = _peaks()[0]
+    out = {}
+
+    # attention backward, this rank's units (strong scaling like the headline)
+    bsets = []
+    for i in range(2):
+        q, k, v = sets[i][:3]
+        do = torch.randn_like(q)
+        o, lse = sa.attention_forward(q, k, v, cm, BS, None, True)
+        bsets.append((q, k, v, o, lse, do, torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)))
+    d = sa._desc(bsets[0][0], bsets[0][1], bsets[0][2], bsets[0][6], cm, None)
+    n = C.c_size_t(0)
+    _lib.check(lib.xsake_attn_bwd_workspace_size(C.byref(d), C.byref(n)))
+    ws = torch.empty(n.value, dtype=torch.uint8, device="cuda")
+    calls = [lambda t=t: lib.xsake_attn_bwd(C.byref(d), cm.plan.data_ptr(), *(x.data_ptr() for x in t),
+                                            ws.data_ptr(), ws.numel(), sp()) for t in bsets]
+    ms = _graph_calls(calls, dist, reps=max(3, args.steps // 4))
+    v_ = n_active(masks, B) * BWD_FLOP_PER_BLOCK / (ms * 1e-3) / 1e12
+    out["attn_bwd"] = {"value": v_, "unit": "TFLOP/s", "ms_per_call": ms, "frac_of_peak": v_ / world / peak_tf,
+                       "work": "10 * D * 64 * 64 FLOPs per active block (S, dP, dV, dK, dQ), whole job"}
+    del bsets
+
+    # softmax config 1a rows split over ranks
+    rows, cols = 8 * 12 * 1024, 1024
+    lo, hi = _split_rows(rows, world, rank)
+    x = torch.randn(hi - lo, cols, device="cuda") * 2
+    r_idx = torch.arange(lo, hi, device="cuda") % cols
+    x.masked_fill_(torch.arange(cols, device="cuda")[None] > r_idx[:, None], float("-inf"))
+    y = torch.empty_like(x)
+    ms = _graph_calls([lambda: lib.xsake_softmax_fwd(0, hi - lo, cols, x.data_ptr(), y.data_ptr(), sp())], dist)
+    gbs = rows * cols * 8 / (ms * 1e-3) / 1e9
+    out["softmax"] = {"value": gbs, "unit": "GB/s", "ms_per_call": ms, "frac_of_hbm_per_gpu": gbs / world / hbm,
+                      "shape": "fp32 [98304, 1024], causal -inf, rows split over ranks"}
+    del x, y
+
+    # layernorm config 1b rows split over ranks (12 rotating inputs so each call reads from HBM)
+    lo, hi = _split_rows(8192, world, rank)
+    xs = [torch.randn(hi - lo, 768, device="cuda").to(torch.bfloat16) for _ in range(12)]
+    gm = 1 + 0.1 * torch.randn(768, device="cuda")
+    bt = 0.1 * torch.randn(768, device="cuda")
+    ys = [torch.empty_like(x) for x in xs]
+    ms = _graph_calls([lambda i=i: lib.xsake_layernorm_fwd(1, hi - lo, 768, xs[i].data_ptr(), gm.data_ptr(),
+                                                           bt.data_ptr(), 1e-5, ys[i].data_ptr(), None, None, sp())
+                       for i in range(12)], dist)
+    gbs = (8192 * 768 * 4 + 2 * 768 * 4) / (ms * 1e-3) / 1e9
+    out["layernorm"] = {"value": gbs, "unit": "GB/s", "ms_per_call": ms, "frac_of_hbm_per_gpu": gbs / world / hbm,
+                        "shape": "bf16 [8192, 768], fp32 gamma/beta, rows split over ranks"}
+    del xs, ys
+
+    # entropy over materialised weights: the [8, 12, 1024, 1024] batch split over ranks
+    lo, hi = _split_rows(8, world, rank)
+    p = torch.softmax(torch.randn(hi - lo, 12, 1024, 1024, device="cuda") * 2, -1)
+    n = C.c_size_t(0)
+    lib.xsake_entropy_workspace_size(hi - lo, 12, 1024, C.byref(n))
+    wse = torch.empty(n.value, dtype=torch.uint8, device="cuda")
+    sums = torch.empty(12, dtype=torch.float64, device="cuda")
+    ms = _graph_calls([lambda: lib.xsake_entropy_rows(p.data_ptr(), hi - lo, 12, 1024, 1024, sums.data_ptr(),
+                                                      wse.data_ptr(), wse.numel(), sp())], dist)
+    gbs = 8 * 12 * 1024 * 1024 * 4 / (ms * 1e-3) / 1e9
+    out["entropy"] = {"value": gbs, "unit": "GB/s", "ms_per_call": ms, "frac_of_hbm_per_gpu": gbs / world / hbm,
+                      "shape": "fp32 P [8, 12, 1024, 1024], batch split over ranks"}
+    del p
+
+    # calibration (config 2): 50 batches of B=8 H=12 S=1024 D=64 fp32 Q, K (Q scaled per head),
+    # round-robin over ranks, fused QK -> entropy, one fp64 all-reduce of the 12 head sums
+    # through the library's NCCL communicator, then every rank builds the masks.
+    Bc, Hc, Sc, Dc, NB = 8, 12, 1024, 64, 50
+    n = C.c_size_t(0)
+    lib.xsake_entropy_qk_workspace_size(Bc, Hc, Sc, C.byref(n))
+    wsq = torch.empty(n.value, dtype=torch.uint8, device="cuda")
+    mine = [i for i in range(NB) if i % world == rank]
+    gen = torch.Generator(device="cuda")
+    tau = torch.linspace(0.25, 4.0, Hc, device="cuda").view(1, Hc, 1, 1)
+    qk = []
+    for i in mine:
+        gen.manual_seed(2000 + i)
+        qk.append(((torch.randn(Bc, Hc, Sc, Dc, device="cuda", generator=gen) * tau).contiguous(),
+                   torch.randn(Bc, Hc, Sc, Dc, device="cuda", generator=gen)))
+    part = torch.empty(Hc, dtype=torch.float64, device="cuda")
+    acc = torch.zeros(Hc, dtype=torch.float64, device="cuda")
+    comm = None
+    if dist is not None:
+        uid = [xcomm.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = xcomm.Comm(uid[0], world, rank)
+        comm.allreduce_sum_f64(torch.zeros(Hc, dtype=torch.float64, device="cuda"))   # connection set-up
+
+    def calib_pass():
+        acc.zero_()
+        for q_, k_ in qk:
+            _lib.check(lib.xsake_entropy_qk(0, q_.data_ptr(), k_.data_ptr(), Bc, Hc, Sc, Dc, 0.125, part.data_ptr(),
+                                            wsq.data_ptr(), wsq.numel(), sp()))
+            acc.add_(part)
+
+    calib_pass()
+    torch.cuda.synchronize()
+    _barrier(dist)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t2 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    calib_pass()
+    t1.record()
+    if comm is not None:
+        comm.allreduce_sum_f64(acc)
+    t2.record()
+    torch.cuda.synchronize()
+    ent = (acc / float(NB * Bc * Sc)).to(torch.float32).cpu().numpy()
+    prof = hp.profile_from_entropies(ent, Sc, 64, causal=True, global_blocks=1)
+    digest = hashlib.blake2b(np.ascontiguousarray(prof.block_masks).tobytes(), digest_size=8).digest()
+    dig = _gather([float(int.from_bytes(digest[:6], "little"))], dist, world)
+    compute_ms = _reduce(t0.elapsed_time(t1), dist, "max")
+    exch_ms = _reduce(t1.elapsed_time(t2), dist, "max")
+    if comm is not None:
+        comm.destroy()
+    fl = 2 * 2 * Bc * Hc * Sc * Sc * Dc * NB
+    out["calibration"] = {"value": fl / ((compute_ms + exch_ms) * 1e-3) / 1e12, "unit": "TFLOP/s",
+                          "batches": NB, "compute_ms": compute_ms, "exchange_ms": exch_ms,
+                          "exchange": "xsake_comm_allreduce_sum_f64 (NCCL) of 12 fp64 head sums" if world > 1
+                          else "none (one rank)",
+                          "masks_equal_across_ranks": all(x == dig[0] for x in dig),
+                          "entropies": [round(float(e), 6) for e in ent],
+                          "shape": "50 batches of fp32 Q, K [8, 12, 1024, 64], round-robin over ranks, fused "
+                                   "QK -> entropy (xsake_entropy_qk)"}
+    return out
 
 
 def run_train(args, dist, rank, world, local):
@@ -394,7 +634,7 @@ def run_train(args, dist, rank, world, local):
         loss = step(batches[i % 2])
     e1.record()
     torch.cuda.synchronize()
-    ms = _max_over_ranks(e0.elapsed_time(e1), dist) / args.steps
+    ms = _reduce(e0.elapsed_time(e1), dist, "max") / args.steps
     # end to end: token ids copied from pinned host memory and the loss read back every step
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n_e2e = max(2, args.steps // 2)
@@ -405,7 +645,7 @@ def run_train(args, dist, rank, world, local):
         lv = float(step(ids).detach().cpu())
     f1.record()
     torch.cuda.synchronize()
-    e2e_ms = _max_over_ranks(f0.elapsed_time(f1), dist) / n_e2e
+    e2e_ms = _reduce(f0.elapsed_time(f1), dist, "max") / n_e2e
     ck = clocks.stop()
     _barrier(dist)
     if rank == 0:
@@ -426,17 +666,16 @@ def run_train(args, dist, rank, world, local):
 
 
 def run_rowop(args, dist, rank, world, local):
-    """Secondary rows (not the headline): softmax / LayerNorm / entropy / attention backward.
-
-    The row kernels are microseconds long, so each is timed as a CUDA graph of 20 direct C-ABI
-    calls on preallocated buffers (no Python or allocation between launches); inputs rotate over
-    enough buffers to exceed the 126 MB L2."""
+    """Single-workload rows (one GPU): softmax / LayerNorm / entropy / calibration / attention
+    backward, each timed as a CUDA graph of 20 direct C-ABI calls on preallocated buffers;
+    inputs rotate over enough buffers to exceed the 126 MB L2 where the call is small."""
     import ctypes as C
     import torch
     from xsake_b200 import _lib, sparse_attention as sa
     lib = _lib.load()
     wl = args.workload
-    sp = lambda: torch.cuda.current_stream().cuda_stream
+    sp = lambda: torch.cuda.current_stream().cuda_stream   # noqa: E731
+    extra = {}
     if wl == "softmax":
         rows, cols = 8 * 12 * 1024, 1024
         x = torch.randn(rows, cols, device="cuda") * 2
@@ -466,7 +705,6 @@ def run_rowop(args, dist, rank, world, local):
                                                 ws.numel(), sp())]
         unit, metric = "GB/s", "HADS entropy over materialised P fp32 [8,12,1024,1024] HBM GB/s"
     elif wl == "calib":
-        # one config-2 calibration batch: B=8 H=12 S=1024 D=64 fp32, q scaled per head, no mask
         Bc, Hc, Sc, Dc = 8, 12, 1024, 64
         tau = torch.linspace(0.25, 4.0, Hc, device="cuda")
         q = torch.randn(Bc, Hc, Sc, Dc, device="cuda") * tau[None, :, None, None]
@@ -478,7 +716,6 @@ def run_rowop(args, dist, rank, world, local):
         nbytes = None
         calls = [lambda: lib.xsake_entropy_qk(0, q.data_ptr(), k.data_ptr(), Bc, Hc, Sc, Dc, 0.125, sums.data_ptr(),
                                               ws.data_ptr(), ws.numel(), sp())]
-        # the drop-in path for comparison: materialised weights, then the entropy reduction
         full = np.ones((1, 16, 16), bool)
         cm = sa.compile_block_mask(full, Bc, Hc, Sc, 64, False, q.device)
         dsc = sa._desc(q, k, k, q, cm, 0.125)
@@ -486,15 +723,15 @@ def run_rowop(args, dist, rank, world, local):
         n2 = C.c_size_t(0)
         lib.xsake_entropy_workspace_size(Bc, Hc, Sc, C.byref(n2))
         ws2 = torch.empty(n2.value, dtype=torch.uint8, device="cuda")
+
         def dropin():
             st = lib.xsake_attn_probs(C.byref(dsc), cm.plan.data_ptr(), q.data_ptr(), k.data_ptr(), pw.data_ptr(), sp())
             return st or lib.xsake_entropy_rows(pw.data_ptr(), Bc, Hc, Sc, Sc, sums.data_ptr(), ws2.data_ptr(),
                                                 ws2.numel(), sp())
+        extra["dropin_ms_per_batch"] = None
         unit, metric = "TFLOP/s", "HADS calibration entropy fused from Q,K (fp32, B=8 H=12 S=1024 D=64) TFLOP/s"
     elif wl == "attn_bwd":
         masks = hads_masks()
-        # two input sets of 151 MB (q, k, v, o, do bf16 + lse) alternate, so each call reads
-        # operands that are not L2-resident from the previous call
         sets = []
         for _ in range(2):
             q, k, v, do = (torch.randn(B, H, S, D, device="cuda").to(torch.bfloat16) for _ in range(4))
@@ -511,54 +748,22 @@ def run_rowop(args, dist, rank, world, local):
         unit, metric = "TFLOP/s", "HADS attn bwd active-block TFLOP/s (bf16 B=4 H=12 S=4096 D=64)"
     else:
         raise SystemExit(f"unknown workload {wl}")
-    use_graph = True
-
-    def run_all():
-        for i in range(20):
-            st = calls[i % len(calls)]()
-            if st:
-                _lib.check(st)
     for _ in range(args.warmup):
-        run_all()
-    torch.cuda.synchronize()
-    if use_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            run_all()
-        replay = graph.replay
-    else:
-        replay = run_all
-    replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        replay()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / (args.steps * 20)
-    extra = {}
+        for c in calls:
+            _lib.check(c())
+    ms = _graph_calls(calls, None, reps=args.steps)
     if wl == "attn_bwd":
-        value = n_active(hads_masks(), B) * 10 * D * 64 * 64 / (ms * 1e-3) / 1e12
+        value = n_active(hads_masks(), B) * BWD_FLOP_PER_BLOCK / (ms * 1e-3) / 1e12
     elif wl == "calib":
         value = 2 * 2 * 8 * 12 * 1024 * 1024 * 64 / (ms * 1e-3) / 1e12
-        for _ in range(3):
-            _lib.check(dropin())
-        torch.cuda.synchronize()
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record()
-        for _ in range(10):
-            _lib.check(dropin())
-        f1.record()
-        torch.cuda.synchronize()
-        extra = {"dropin_ms_per_batch": f0.elapsed_time(f1) / 10, "fused_ms_per_batch": ms,
-                 "dropin": "xsake_attn_probs (403 MB of fp32 weights) + xsake_entropy_rows"}
+        extra = {"dropin_ms_per_batch": _time_calls(lambda: _lib.check(dropin()), 10, None),
+                 "fused_ms_per_batch": ms, "dropin": "xsake_attn_probs (403 MB of fp32 weights) + xsake_entropy_rows"}
     else:
         value = nbytes / (ms * 1e-3) / 1e9
     _, hbm, kind = _peaks()
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps * 20,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "config": {"workload": wl, "timing": "CUDA graph of 20 calls" if use_graph else "eager"},
+            "config": {"workload": wl, "timing": "CUDA graph of 20 calls"},
             "note": "secondary row; not the headline"}
     line.update(extra)
     if wl == "calib":
@@ -584,8 +789,10 @@ def main():
     ap.add_argument("--steps", type=int, default=3000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="xsake", choices=["xsake", "reference"])
-    ap.add_argument("--workload", default="attn", choices=["attn", "attn_bwd", "calib", "train", "softmax", "layernorm", "entropy"])
+    ap.add_argument("--workload", default="attn",
+                    choices=["attn", "attn_bwd", "calib", "train", "softmax", "layernorm", "entropy"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="headline only (no backward/row/calibration fields)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":

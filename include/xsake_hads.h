@@ -71,10 +71,46 @@ typedef struct {
 XSAKE_API int xsake_mask_plan_bytes(const XsakeMaskDims* dims, size_t* bytes);
 XSAKE_API int xsake_mask_compile(const XsakeMaskDims* dims, const uint8_t* mask_dev, void* plan_dev,
                        size_t plan_bytes, void* stream);
+
+/* Options of xsake_mask_compile_ex (the reference has no counterpart: it runs one job per device,
+ * distributed/pmap_trainer.py:32-68).  units_dev (device memory, NULL = every unit) lists the
+ * (b, h) units, as b * heads + h, that calls with this plan compute: a job whose batch x heads
+ * is sharded over GPUs compiles on each rank a plan of its own units, and the attention calls
+ * read and write only those units' rows of q, k, v, o, lse and the gradients.  workers is the
+ * number of tile workers the forward runs concurrently (0 = 2 x the SM count of the current
+ * device); the plan splits a query tile's kv walk into pieces when it is long next to the
+ * average load of a worker, so a small job still fills the GPU.  Invalid unit ids are left out
+ * and recorded in the device error word. */
+typedef struct {
+  const int32_t* units_dev;
+  int32_t n_units;
+  int32_t workers;
+} XsakePlanOptions;
+
+XSAKE_API int xsake_mask_compile_ex(const XsakeMaskDims* dims, const XsakePlanOptions* options,
+                       const uint8_t* mask_dev, void* plan_dev, size_t plan_bytes, void* stream);
+
 /* Copies the plan's summary to host (synchronises `stream`): out[0] = active (q-block,
- * kv-block) pairs after the causal cut over B*H, out[1] = 64x64 tiles the forward
- * computes, out[2] = fully masked q-blocks, out[3] = forward work items. */
+ * kv-block) pairs after the causal cut over the selected units, out[1] = 64x64 tiles the
+ * forward computes with the pairing the plan chose, out[2] = fully masked q-blocks,
+ * out[3] = forward work items. */
 XSAKE_API int xsake_mask_plan_stats(const void* plan_dev, void* stream, int64_t out[4]);
+
+/* The same summary and the plan compiler's choices (synchronises `stream`). */
+typedef struct {
+  int64_t active_blocks;    /* active (q-block, kv-block) pairs after the causal cut      */
+  int64_t computed_tiles;   /* 64x64 tiles the tensor-core forward computes               */
+  int64_t empty_qblocks;    /* fully masked q-blocks                                       */
+  int32_t work_items;       /* forward work items, split pieces included                   */
+  int32_t selected_units;   /* (b, h) units the plan computes                              */
+  int32_t unit_pairing;     /* 1: the forward pairs two units per item, 0: two query chunks */
+  int32_t split_items;      /* work items cut into pieces over their kv chunks             */
+  int32_t split_slots;      /* partial slots those pieces use                              */
+  int32_t split_cap;        /* largest piece, in 64-key chunks                             */
+  int32_t workers;          /* tile workers the split rule assumed                         */
+  int32_t reserved;
+} XsakePlanInfo;
+XSAKE_API int xsake_mask_plan_info(const void* plan_dev, void* stream, XsakePlanInfo* info);
 
 /* ------------------------------------------------------------------ attention
  * Replaces sparse_attention / sparse_attention_pallas / _sparse_attn_fwd_kernel
@@ -96,6 +132,9 @@ typedef struct {
   int64_t o_stride[3];      /* also used for do, dq, dk, dv                           */
 } XsakeAttnDesc;
 
+/* The forward's workspace (256-byte aligned) holds the work-item counter and, for the tensor-core
+ * path, the partial results of split work items (about 17 MB); its first bytes are reset on the
+ * stream by every call.  Only rows of the units the plan selects are written. */
 XSAKE_API int xsake_attn_fwd_workspace_size(const XsakeAttnDesc* desc, size_t* bytes);
 XSAKE_API int xsake_attn_fwd(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
                    const void* k_dev, const void* v_dev, void* o_dev, float* lse_dev,

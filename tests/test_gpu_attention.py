@@ -142,13 +142,21 @@ def test_bf16_dense_mask_several_units():
 
 
 def test_forward_pairing_follows_the_mask():
-    # Header word 24 of the plan (H_FWD_PAIR): unit pairing for HADS masks shared by 4 units,
-    # query-chunk pairing for one unit per mask and for a dense causal mask.
+    # Unit pairing for HADS masks shared by 4 units, query-chunk pairing for one unit per mask
+    # and for a dense causal mask, at block 64 and block 128 (the choice counts useful 64-row
+    # halves, whatever the block size).
     sa = _sa()
     hads = oh.dummy_hads_profile(12, 4096, 64, causal=True, global_blocks=1).block_masks
-    for m, B, want in [(hads, 4, 1), (hads, 1, 0), (np.ones((64, 64), bool), 4, 0)]:
-        cm = sa.compile_block_mask(m, B, 12, 4096, 64, True)
-        assert int(cm.plan.view(torch.int32)[24].item()) == want, (B, want)
+    cases = [(hads, 4, 64, "unit"), (hads, 1, 64, "query_chunk"), (np.ones((64, 64), bool), 4, 64, "query_chunk"),
+             (np.ones((32, 32), bool), 4, 128, "query_chunk")]
+    for m, B, bs, want in cases:
+        cm = sa.compile_block_mask(m, B, 12, 4096, bs, True)
+        st = cm.stats()
+        assert st["pairing"] == want, (B, bs, want)
+        # computed tiles follow the chosen pairing: every useful half once for unit pairing
+        if bs == 64 and want == "unit":
+            assert st["computed_tiles"] == oa.active_block_count(m, B, 12, 4096 // bs, True)
+        assert st["computed_tiles"] >= st["active_blocks"]
 
 
 def test_bf16_bshd_layout_and_scale():
@@ -340,8 +348,33 @@ def test_plan_mismatch_is_reported_not_faulted():
     lib = _lib.load()
     stream = sa.dev.stream_ptr()
     _lib.device_error(stream)                            # clear earlier words
-    ws = torch.zeros(256, dtype=torch.uint8, device="cuda")
+    n = C.c_size_t(0)
+    _lib.check(lib.xsake_attn_fwd_workspace_size(C.byref(d), C.byref(n)))
+    ws = torch.zeros(n.value, dtype=torch.uint8, device="cuda")
     _lib.check(lib.xsake_attn_fwd(C.byref(d), cm.plan.data_ptr(), q.data_ptr(), q.data_ptr(),
-                                  q.data_ptr(), o.data_ptr(), lse.data_ptr(), ws.data_ptr(), 256, stream))
+                                  q.data_ptr(), o.data_ptr(), lse.data_ptr(), ws.data_ptr(), ws.numel(), stream))
     code = _lib.device_error(stream)
     assert code >> 24 == 2
+
+
+def test_cuda_mask_cache_follows_content():
+    """Plans are cached by mask content: a freed bool CUDA mask whose address the caching
+    allocator hands to a different mask, and a mask written in place through .data, each get the
+    plan of their own content."""
+    sa = _sa()
+    B, H, S, bs = 1, 2, 256, 64
+    q, k, v = (_bf16_round(_rand((B, H, S, 64), 400 + i)) for i in range(3))
+    tq, tk, tv = (torch.from_numpy(x).to(torch.bfloat16).cuda() for x in (q, k, v))
+    first = np.zeros((H, 4, 4), bool)
+    first[:, :, 0] = True
+    m1 = torch.from_numpy(first).cuda()
+    o1, _ = sa.attention_forward(tq, tk, tv, m1, bs, None, True)
+    del m1
+    m2 = torch.ones((H, 4, 4), dtype=torch.bool, device="cuda")      # typically the freed address
+    o2, _ = sa.attention_forward(tq, tk, tv, m2, bs, None, True)
+    ref2, _ = oa.sparse_attention_reference(q, k, v, np.ones((H, 4, 4), bool), bs, causal=True,
+                                            return_weights=False)
+    assert _err(o2.float().cpu().numpy(), ref2) <= BF16_TOL * np.abs(ref2).max()
+    m2.data.copy_(torch.from_numpy(first).cuda())                    # in place: _version unchanged
+    o3, _ = sa.attention_forward(tq, tk, tv, m2, bs, None, True)
+    assert torch.equal(o3, o1)

@@ -53,6 +53,16 @@ def to_device(x, dtype=None):
     return t, was_host
 
 
+def host_tensor(a) -> "torch.Tensor":
+    """A CPU torch view of a host array (NumPy bfloat16 viewed through int16, bool as uint8)."""
+    a = np.asarray(a)
+    if a.dtype == _bf16_np():
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
+    if a.dtype == np.bool_:
+        return torch.from_numpy(np.ascontiguousarray(a).astype(np.uint8))
+    return torch.from_numpy(np.ascontiguousarray(a))
+
+
 def to_host(t: "torch.Tensor"):
     t = t.detach()
     if t.dtype == torch.bfloat16:

@@ -30,6 +30,17 @@ class MaskDims(C.Structure):
                 ("block_size", C.c_int32), ("causal", C.c_int32)]
 
 
+class PlanOptions(C.Structure):
+    _fields_ = [("units_dev", C.c_void_p), ("n_units", C.c_int32), ("workers", C.c_int32)]
+
+
+class PlanInfo(C.Structure):
+    _fields_ = [("active_blocks", C.c_int64), ("computed_tiles", C.c_int64), ("empty_qblocks", C.c_int64),
+                ("work_items", C.c_int32), ("selected_units", C.c_int32), ("unit_pairing", C.c_int32),
+                ("split_items", C.c_int32), ("split_slots", C.c_int32), ("split_cap", C.c_int32),
+                ("workers", C.c_int32), ("reserved", C.c_int32)]
+
+
 class AttnDesc(C.Structure):
     _fields_ = [("dtype", C.c_int32), ("batch", C.c_int32), ("heads", C.c_int32),
                 ("seq", C.c_int32), ("head_dim", C.c_int32), ("block_size", C.c_int32),
@@ -47,7 +58,9 @@ _SIGS = {
     "xsake_device_error": (C.c_int, [_VP, C.POINTER(_I32)]),
     "xsake_mask_plan_bytes": (C.c_int, [C.POINTER(MaskDims), C.POINTER(_SZ)]),
     "xsake_mask_compile": (C.c_int, [C.POINTER(MaskDims), _VP, _VP, _SZ, _VP]),
+    "xsake_mask_compile_ex": (C.c_int, [C.POINTER(MaskDims), C.POINTER(PlanOptions), _VP, _VP, _SZ, _VP]),
     "xsake_mask_plan_stats": (C.c_int, [_VP, _VP, C.POINTER(_I64)]),
+    "xsake_mask_plan_info": (C.c_int, [_VP, _VP, C.POINTER(PlanInfo)]),
     "xsake_attn_fwd_workspace_size": (C.c_int, [C.POINTER(AttnDesc), C.POINTER(_SZ)]),
     "xsake_attn_fwd": (C.c_int, [C.POINTER(AttnDesc), _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "xsake_attn_bwd_workspace_size": (C.c_int, [C.POINTER(AttnDesc), C.POINTER(_SZ)]),

@@ -81,6 +81,26 @@ def unit_costs(block_masks: np.ndarray, batch: int, causal: bool = True) -> np.n
     return np.tile(per_head, batch)                     # unit u = b * H + h
 
 
+def pair_shard(block_masks: np.ndarray, batch: int, world: int, causal: bool = True) -> List[List[int]]:
+    """Units ``b * H + h`` of each rank when one job's batch x heads is split over ``world``
+    ranks, for per-head masks ``[H, nq, nk]`` shared by the batch.  Such a mask lets the forward
+    compute two batch units of one head per work item, so units are assigned two at a time
+    ((b, b+1) of one head, a lone unit when the batch is odd), longest first by active blocks
+    (heads differ ~5x in density); each rank's list is ascending."""
+    m = np.asarray(block_masks, bool)
+    if m.ndim != 3:
+        raise ValueError(f"pair_shard needs per-head masks [H, nq, nk], got shape {m.shape}")
+    heads = m.shape[0]
+    costs = unit_costs(m, batch, causal)
+    jobs = [[b * heads + h for b in range(b0, min(b0 + 2, batch))]
+            for h in range(heads) for b0 in range(0, batch, 2)]
+    out: List[List[int]] = [[] for _ in range(world)]
+    for r, idx in enumerate(lpt_shard([float(sum(costs[u] for u in j)) for j in jobs], world)):
+        for i in idx:
+            out[r].extend(jobs[i])
+    return [sorted(x) for x in out]
+
+
 def lpt_shard(costs: Sequence[float], world: int) -> List[List[int]]:
     """Longest-processing-time-first assignment of units to ``world`` ranks (deterministic:
     ties broken by unit index and rank index)."""

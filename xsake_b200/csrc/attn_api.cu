@@ -51,7 +51,11 @@ using namespace xsake;
 extern "C" int xsake_attn_fwd_workspace_size(const XsakeAttnDesc* desc, size_t* bytes) {
   clear_error();
   XSAKE_REQUIRE(desc && bytes, XSAKE_EINVAL, "NULL argument");
-  *bytes = 256;   // work-item counter of the persistent tensor-core kernel
+  // Work-item counter and split-piece partials of the persistent tensor-core kernel; the
+  // CUDA-core kernels need none.
+  const bool tc = desc->dtype == XSAKE_BF16 && desc->head_dim == 64 && desc->block_size > 0 &&
+                  desc->block_size % 64 == 0 && desc->seq % 64 == 0;
+  *bytes = tc ? tc_attn_fwd_workspace() : 256;
   return XSAKE_OK;
 }
 

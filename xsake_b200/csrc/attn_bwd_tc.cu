@@ -253,7 +253,7 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
       uint32_t g = 0, j = 0;
       bool ok = true;
       for (uint32_t k = 0; ok; ++k) {
-        const int item = publish_item(bars, item_slot, k, p.counter, items, L.nitems, abort);
+        const int item = publish_item(bars, item_slot, k, p.counter, items, a.plan[H_B_ITEMS], abort);
         if (item == -2) { ok = false; break; }
         if (item < 0) break;
         const Item w = decode(a, rowptr, item);
@@ -550,7 +550,7 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       uint32_t g = 0, j = 0;
       bool ok = true;
       for (uint32_t k = 0; ok; ++k) {
-        const int item = publish_item(bars, item_slot, k, p.counter + 1, items, L.nitems, abort);
+        const int item = publish_item(bars, item_slot, k, p.counter + 1, items, a.plan[H_F_ITEMS], abort);
         if (item == -2) { ok = false; break; }
         if (item < 0) break;
         const Item w = decode(a, rowptr, item);
@@ -770,6 +770,7 @@ __global__ void __launch_bounds__(256) tc_bwd_prep_kernel(AttnArgs a, float* __r
     const int s = (int)(row % a.S);
     const int64_t bh = row / a.S;
     const int b = (int)(bh / a.H), h = (int)(bh % a.H);
+    if (!plan_unit_selected(a.plan, a.L, b, h)) return;   // warp-uniform: 4 rows of one unit
     const int64_t off = b * a.os[0] + h * a.os[1] + (int64_t)s * a.os[2] + 8 * sub;
     const uint4 o = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.o) + off);
     const uint4 d = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.dout) + off);
@@ -795,6 +796,7 @@ __global__ void __launch_bounds__(256) tc_bwd_prep_kernel(AttnArgs a, float* __r
 // ucol[b, h, d] = (1/S) * sum of dO over the rows of fully masked q-blocks (0 when none).
 __global__ void __launch_bounds__(64) tc_ucol_kernel(AttnArgs a) {
   const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+  if (!plan_unit_selected(a.plan, a.L, b, h)) return;
   const int c = threadIdx.x;
   const uint8_t* qe =
       reinterpret_cast<const uint8_t*>(a.plan + a.L.qempty_off) + (int64_t)a.L.group_of(b, h) * a.L.nq;

@@ -41,7 +41,7 @@ __device__ __forceinline__ bool plan_matches(const AttnArgs& a) {
 int simt_attn_fwd(const AttnArgs& a, int dtype, cudaStream_t s);
 int simt_attn_bwd(const AttnArgs& a, int dtype, cudaStream_t s);
 int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
-size_t tc_attn_fwd_workspace(const AttnArgs& a);
+size_t tc_attn_fwd_workspace();   // bytes the tensor-core forward needs
 bool tc_attn_fwd_supported(const AttnArgs& a, int dtype);
 int tc_attn_bwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
 bool tc_attn_bwd_supported(const AttnArgs& a, int dtype);

@@ -77,6 +77,7 @@ struct Bars {
   uint64_t p_full[2][3];                 // [tile][S buffer holding P]
   uint64_t o_done[2][2];                 // [tile][PV parity]
   uint64_t o_free[2];
+  uint64_t ep_bar[2];                    // [tile]: the softmax warpgroup's split-merge rendezvous
   uint64_t drain;
 };
 constexpr int kOffMisc = kOffBar + (int)sizeof(Bars);
@@ -91,7 +92,9 @@ constexpr int kItemReaders = 1 + 128;                 // the tile's MMA warp + i
 struct TcParams {
   AttnArgs a;
   float scale_log2;
-  int* counter;   // zeroed by the host before the launch
+  int* counter;       // work-item counter, zeroed by the host before the launch
+  int* grp_counter;   // [kSplitSlots] pieces finished per split group, zeroed with the counter
+  float* parts;       // [kSplitSlots] partial slots of split pieces (kSlotFloats each)
 };
 
 __device__ __forceinline__ void fail(volatile int* abort, int detail) {
@@ -123,21 +126,125 @@ __device__ void warp_mean_v(const AttnArgs& a, int b, int h, float2& mine) {
   mine = make_float2(s0 / a.S, s1 / a.S);
 }
 
+// Entry `idx` of the plan's forward work table (two 16-byte loads).
+__device__ __forceinline__ FWork load_work(const AttnArgs& a, int idx) {
+  const int4* w = reinterpret_cast<const int4*>(a.plan + a.L.f_work_off) + 2 * (int64_t)idx;
+  const int4 x = w[0], y = w[1];
+  FWork f;
+  f.u0 = x.x; f.u1 = x.y; f.q = x.z; f.lo = x.w;
+  f.hi = y.x; f.parts = y.y; f.grp = y.z; f.slot = y.w;
+  return f;
+}
+
 struct Item {
   int b, h, u, e0, n;
 };
 
-__device__ __forceinline__ Item decode(const AttnArgs& a, const int32_t* rowptr, int item) {
-  const PlanLayout& L = a.L;
+// The softmax warps hold a work entry spread over lanes 0-7 (lane i: word i of FWork), one
+// register a thread, and shuffle fields out where they are used.
+__device__ __forceinline__ int32_t work_lanes(const AttnArgs& a, int idx) {
+  const int lane = threadIdx.x & 31;
+  return lane < 8 ? a.plan[a.L.f_work_off + 8 * (int64_t)idx + lane] : 0;
+}
+__device__ __forceinline__ int32_t work_word(int32_t held, int i) { return __shfl_sync(0xffffffffu, held, i); }
+
+
+__device__ __forceinline__ Item decode(const AttnArgs& a, int idx) {
+  const FWork w = load_work(a, idx);
   Item it;
-  it.u = item % L.npairs;
-  const int bh = item / L.npairs;
-  it.b = bh / a.H;
-  it.h = bh % a.H;
-  const int r = L.group_of(it.b, it.h) * L.npairs + it.u;
-  it.e0 = rowptr[r];
-  it.n = rowptr[r + 1] - it.e0;
+  it.u = w.q;
+  it.b = w.u0 / a.H;
+  it.h = w.u0 % a.H;
+  it.e0 = w.lo;
+  it.n = w.hi - w.lo;
   return it;
+}
+
+// Split pieces.  A piece of a split work item leaves its rows' unnormalised O, running max
+// (log2 units) and row sum in its partial slot ([16][128][4] floats of O, then m[128], l[128]);
+// the worker's 128 softmax threads meet on ep_bar (bounded waits), one of them counts the piece
+// done, and the piece that completes its group merges every slot of the group in piece order,
+// so the result does not depend on which piece finished last.
+constexpr int kSlotFloats = 128 * 64 + 2 * 128;
+
+// Returns true when this piece was the group's last and m, l, o now hold the merged row.
+__device__ __forceinline__ bool split_finish(const TcParams& p, int grp, int part, int nparts, int slot0, int srow,
+                                             uint64_t* ep_bar, uint32_t& ep_phase, volatile int* flag, float& m,
+                                             float& l, float (&o)[64], volatile int* abort, bool& ok) {
+  float* mine = p.parts + (int64_t)(slot0 + part) * kSlotFloats;
+  float4* ob = reinterpret_cast<float4*>(mine);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) ob[k * 128 + srow] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+  mine[128 * 64 + srow] = m;
+  mine[128 * 64 + 128 + srow] = l;
+  // The warpgroup's stores are ordered before one thread's gpu-scope release by the CTA-scope
+  // rendezvous (the pattern of a grid barrier: only the counting thread fences); the counting
+  // thread's acquire orders the merge's loads after the other pieces' stores, and the second
+  // rendezvous hands that order to the warpgroup.
+  mbar_arrive(ep_bar);
+  if (!warp_mbar_wait(ep_bar, ep_phase & 1, abort)) { ok = false; return false; }
+  ++ep_phase;
+  if (srow == 0) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(p.grp_counter + grp) : "memory");
+    *flag = old == nparts - 1;
+  }
+  mbar_arrive(ep_bar);
+  if (!warp_mbar_wait(ep_bar, ep_phase & 1, abort)) { ok = false; return false; }
+  ++ep_phase;
+  if (!*flag) return false;
+  float M = -INFINITY;
+  for (int q = 0; q < nparts; ++q) {
+    const float* pq = p.parts + (int64_t)(slot0 + q) * kSlotFloats;
+    if (__ldcg(pq + 128 * 64 + 128 + srow) > 0.f) M = fmaxf(M, __ldcg(pq + 128 * 64 + srow));
+  }
+  float lt = 0.f;
+#pragma unroll
+  for (int c = 0; c < 64; ++c) o[c] = 0.f;
+  for (int q = 0; q < nparts; ++q) {
+    const float* pq = p.parts + (int64_t)(slot0 + q) * kSlotFloats;
+    const float lq = __ldcg(pq + 128 * 64 + 128 + srow);
+    if (!(lq > 0.f)) continue;
+    const float f = ex2(__ldcg(pq + 128 * 64 + srow) - M);
+    lt += lq * f;
+    const float4* oq = reinterpret_cast<const float4*>(pq);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float4 v = __ldcg(oq + k * 128 + srow);
+      o[4 * k] += v.x * f;
+      o[4 * k + 1] += v.y * f;
+      o[4 * k + 2] += v.z * f;
+      o[4 * k + 3] += v.w * f;
+    }
+  }
+  m = M;
+  l = lt;
+  return true;
+}
+
+// The row's O accumulator (64 fp32 columns at TMEM column `taddr`) into registers.
+__device__ __forceinline__ void load_o_row(uint32_t taddr, float (&o)[64]) {
+  uint32_t r[64];
+  XSAKE_TMEM_LD32(taddr, r);
+  XSAKE_TMEM_LD32(taddr + 32, (r + 32));
+  XSAKE_TMEM_WAIT_LD32(r);
+  XSAKE_TMEM_WAIT_LD32((r + 32));
+#pragma unroll
+  for (int j = 0; j < 64; ++j) o[j] = __uint_as_float(r[j]);
+}
+
+// One bf16 output row: o * inv, eight 16-byte stores.
+__device__ __forceinline__ void store_o_row(uint4* orow_g, const float (&o)[64], float inv) {
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc) {
+    uint32_t wv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      __nv_bfloat162 pb = __floats2bfloat162_rn(o[8 * cc + 2 * q] * inv, o[8 * cc + 2 * q + 1] * inv);
+      wv[q] = *reinterpret_cast<uint32_t*>(&pb);
+    }
+    orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
 }
 
 // Entry i of an item's list for a whole warp.  The list is read 32 entries at a time into lane
@@ -160,8 +267,8 @@ struct FwdCtx {
   Bars* bars;
   volatile int* abort;
   volatile int* item_slots;   // [tile worker][slot]
+  volatile int* ep_flag;      // [tile worker]: this piece completed its split group
   uint32_t tmem;
-  const int32_t* rowptr;
   const int32_t* entries;
 };
 
@@ -173,12 +280,11 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
   volatile int* abort = c.abort;
   volatile int* item_slots = c.item_slots;
   const uint32_t tmem = c.tmem;
-  const int32_t* rowptr = c.rowptr;
   const int32_t* entries = c.entries;
   const AttnArgs& a = p.a;
   const PlanLayout& L = a.L;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int32_t* items = a.plan + L.f_items_off;
+  const int nwork = a.plan[H_F_WORK];
   if (warp == 8 || warp == 9) {
     // ------------------------------------------------------------------ scheduler + TMA
     // One warp per tile (X = warp - 8); the whole warp runs the (uniform) control flow, one
@@ -192,16 +298,16 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
       const int slot = k & 1;
       if (!warp_mbar_wait(&bars->item_empty[X][slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
       int idx = 0;
-      if (lane == 0) idx = *abort ? L.nitems : atomicAdd(p.counter, 1);
+      if (lane == 0) idx = *abort ? nwork : atomicAdd(p.counter, 1);
       idx = __shfl_sync(0xffffffffu, idx, 0);
-      const int item = idx < L.nitems ? items[idx] : -1;
+      const int item = idx < nwork ? idx : -1;
       if (elect_one()) {
         item_slot[slot] = item;
         mbar_arrive(&bars->item_full[X][slot]);
       }
       __syncwarp();
       if (item < 0) break;
-      const Item w = decode(a, rowptr, item);
+      const Item w = decode(a, item);
       if (w.n == 0) continue;
       const int qs = qk % kQSlots;
       if (!warp_mbar_wait(&bars->q_empty[X][qs], ((qk / kQSlots) & 1) ^ 1, abort)) { ok = false; break; }
@@ -283,7 +389,7 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
       if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
       __syncwarp();
       if (item < 0) break;
-      const Item w = decode(a, rowptr, item);
+      const Item w = decode(a, item);
       if (w.n == 0) continue;
       const int qs = qk % kQSlots;
       if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
@@ -383,6 +489,7 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
     uint64_t* o_free = &bars->o_free[X];
     uint32_t it = 0, sb_c = 0, ph_c = 0;   // step count, its S buffer (it % 3) and phase ((it / 3) & 1)
     bool s_ready = false;                  // S of step `it` already seen complete by every lane
+    uint32_t ep_phase = 0;                 // uses of ep_bar[X]
     bool ok = true;
     for (uint32_t k = 0; ok; ++k) {
       const int slot = k & 1;
@@ -390,12 +497,13 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
       const int item = item_slot[slot];
       mbar_arrive(&bars->item_empty[X][slot]);
       if (item < 0) break;
-      const Item w = decode(a, rowptr, item);
+      const int32_t wk = work_lanes(a, item);
+      const int we0 = work_word(wk, 3), wn = work_word(wk, 4) - we0;
       float m = -INFINITY, l = 0.f;
       int nsteps = 0;
       // The item's entries, 32 at a time: a ballot marks them and a shuffle hands each one out.
-      for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
-        const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
+      for (int b0 = 0; b0 < wn && ok; b0 += 32) {
+        const int32_t eb = b0 + lane < wn ? entries[we0 + b0 + lane] : 0;
         uint32_t own = __ballot_sync(0xffffffffu, (eb & f_tile) != 0);
         while (own) {
           const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
@@ -497,11 +605,7 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
       }
       if (!ok) break;
       // ---------------------------------------------------------------- epilogue
-      const int tok = 128 * w.u + row;
-      const bool valid = tok < a.S;
-      const bool empty = valid && !(l > 0.f);
-      uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + w.b * a.os[0] +
-                                               w.h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
+      float o[64];
       if (nsteps > 0) {
         // PV(s) completes phase s/2 of o_done[s % 2].  A parity wait for PV(it-1) is only
         // unambiguous if that barrier's previous phase (PV(it-3)) has completed; the last S
@@ -511,33 +615,31 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
         if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
         if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
         tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-        for (int hcol = 0; hcol < 2; ++hcol) {
-          uint32_t orow[32];
-          XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
-          XSAKE_TMEM_WAIT_LD32(orow);
-          if (valid && !empty) {
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-              uint32_t wv[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                __nv_bfloat162 pb = __floats2bfloat162_rn(__uint_as_float(orow[8 * cc + 2 * q]) * inv,
-                                                          __uint_as_float(orow[8 * cc + 2 * q + 1]) * inv);
-                wv[q] = *reinterpret_cast<uint32_t*>(&pb);
-              }
-              orow_g[4 * hcol + cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-            }
-          }
-        }
+        load_o_row(tcol + lane_base + 192, o);
         tc_fence_before();
         mbar_arrive(o_free);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) o[j] = 0.f;
       }
+      const int grp = work_word(wk, 6), parts = work_word(wk, 5);
+      if (grp >= 0 && !split_finish(p, grp, parts >> 8, parts & 0xff, work_word(wk, 7), row, &bars->ep_bar[X],
+                                    ep_phase, c.ep_flag + X, m, l, o, abort, ok)) {
+        if (!ok) break;
+        continue;   // another piece of this item merges the rows
+      }
+      const int u0 = work_word(wk, 0);
+      const Item we{u0 / a.H, u0 % a.H, work_word(wk, 2), 0, 0};
+      const int tok = 128 * we.u + row;
+      const bool valid = tok < a.S;
+      const bool empty = valid && !(l > 0.f);
+      uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + we.b * a.os[0] +
+                                               we.h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
+      if (valid && !empty) store_o_row(orow_g, o, 1.f / l);
       if (__any_sync(0xffffffffu, empty)) {
         // Rows with no live score: the reference's finfo.min fill makes them attend uniformly.
         float2 mine;
-        warp_mean_v(a, w.b, w.h, mine);
+        warp_mean_v(a, we.b, we.h, mine);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           uint32_t wv[4];
@@ -551,7 +653,7 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
           if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
         }
       }
-      if (valid) a.lse[(int64_t)(w.b * a.H + w.h) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
+      if (valid) a.lse[(int64_t)(we.b * a.H + we.h) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
     }
     if (!ok) fail(abort, 4);
   }
@@ -584,30 +686,18 @@ struct PItem {
   bool solo;
 };
 
-__host__ __device__ __forceinline__ int pair_units(const PlanLayout& L, int B, int H) {
-  return (L.Bm == 1 ? B : 1) * (L.Hm == 1 ? H : 1);
-}
-__host__ __device__ __forceinline__ int pair_items(const PlanLayout& L, int B, int H) {
-  return L.n64 * L.Bm * L.Hm * ((pair_units(L, B, H) + 1) / 2);
-}
-
-__device__ __forceinline__ PItem decode_pair(const AttnArgs& a, const int32_t* rowptr, int item) {
-  const PlanLayout& L = a.L;
-  const int fh = L.Hm == 1 ? a.H : 1;
-  const int U = pair_units(L, a.B, a.H), P = (U + 1) / 2, per_j = L.Bm * L.Hm * P;
+__device__ __forceinline__ PItem decode_pair(const AttnArgs& a, int idx) {
+  const FWork w = load_work(a, idx);
   PItem it;
-  it.j = L.n64 - 1 - item / per_j;
-  const int rem = item % per_j, g = rem / P, u0 = 2 * (rem % P);
-  it.solo = u0 + 1 >= U;
-  const int u1 = it.solo ? u0 : u0 + 1;
-  const int gb = L.Bm == 1 ? 0 : g / L.Hm, gh = L.Hm == 1 ? 0 : g % L.Hm;
-  it.b0 = L.Bm == 1 ? u0 / fh : gb;
-  it.h0 = L.Hm == 1 ? u0 % fh : gh;
-  it.b1 = L.Bm == 1 ? u1 / fh : gb;
-  it.h1 = L.Hm == 1 ? u1 % fh : gh;
-  const int r = g * L.npairs + (it.j >> 1);
-  it.e0 = rowptr[r];
-  it.n = rowptr[r + 1] - it.e0;
+  it.j = w.q;
+  it.solo = w.u1 < 0;
+  const int u1 = it.solo ? w.u0 : w.u1;
+  it.b0 = w.u0 / a.H;
+  it.h0 = w.u0 % a.H;
+  it.b1 = u1 / a.H;
+  it.h1 = u1 % a.H;
+  it.e0 = w.lo;
+  it.n = w.hi - w.lo;
   return it;
 }
 
@@ -644,12 +734,11 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
   volatile int* abort = c.abort;
   volatile int* item_slots = c.item_slots;
   const uint32_t tmem = c.tmem;
-  const int32_t* rowptr = c.rowptr;
   const int32_t* entries = c.entries;
   const AttnArgs& a = p.a;
   const PlanLayout& L = a.L;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nitems = pair_items(L, a.B, a.H);
+  const int nwork = a.plan[H_F_WORK];
   if (warp == 8 || warp == 9) {
     // ------------------------------------------------------------------ scheduler + TMA
     const int X = warp - 8;
@@ -661,16 +750,16 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       const int slot = k & 1;
       if (!warp_mbar_wait(&bars->item_empty[X][slot], ((k >> 1) & 1) ^ 1, abort)) { ok = false; break; }
       int idx = 0;
-      if (lane == 0) idx = *abort ? nitems : atomicAdd(p.counter, 1);
+      if (lane == 0) idx = *abort ? nwork : atomicAdd(p.counter, 1);
       idx = __shfl_sync(0xffffffffu, idx, 0);
-      const int item = idx < nitems ? idx : -1;
+      const int item = idx < nwork ? idx : -1;
       if (elect_one()) {
         item_slot[slot] = item;
         mbar_arrive(&bars->item_full[X][slot]);
       }
       __syncwarp();
       if (item < 0) break;
-      const PItem w = decode_pair(a, rowptr, item);
+      const PItem w = decode_pair(a, item);
       const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
       int last = -1;
       if (count_steps(entries, w.e0, w.n, fa, last) == 0) continue;
@@ -780,7 +869,7 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
       __syncwarp();
       if (item < 0) break;
-      const PItem w = decode_pair(a, rowptr, item);
+      const PItem w = decode_pair(a, item);
       const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
       int last_used = -1;
       if (count_steps(entries, w.e0, w.n, fa, last_used) == 0) continue;
@@ -857,6 +946,7 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
     uint64_t* o_free = &bars->o_free[X];
     uint32_t it = 0, sb_c = 0, ph_c = 0;
     bool s_ready = false;
+    uint32_t ep_phase = 0;                 // uses of ep_bar[X]
     bool ok = true;
     for (uint32_t k = 0; ok; ++k) {
       const int slot = k & 1;
@@ -864,14 +954,15 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       const int item = item_slot[slot];
       mbar_arrive(&bars->item_empty[X][slot]);
       if (item < 0) break;
-      const PItem w = decode_pair(a, rowptr, item);
-      const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
-      const int32_t fd = (w.j & 1) ? kFlagDiag1 : kFlagDiag0;
-      const bool live = !(w.solo && upper);
+      const int32_t wk = work_lanes(a, item);
+      const int we0 = work_word(wk, 3), wn = work_word(wk, 4) - we0, wj = work_word(wk, 2);
+      const int32_t fa = (wj & 1) ? kFlagActive1 : kFlagActive0;
+      const int32_t fd = (wj & 1) ? kFlagDiag1 : kFlagDiag0;
+      const bool live = !(work_word(wk, 1) < 0 && upper);
       float m = -INFINITY, l = 0.f;
       int nsteps = 0;
-      for (int b0 = 0; b0 < w.n && ok; b0 += 32) {
-        const int32_t eb = b0 + lane < w.n ? entries[w.e0 + b0 + lane] : 0;
+      for (int b0 = 0; b0 < wn && ok; b0 += 32) {
+        const int32_t eb = b0 + lane < wn ? entries[we0 + b0 + lane] : 0;
         uint32_t own = __ballot_sync(0xffffffffu, (eb & fa) != 0);
         while (own) {
           const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
@@ -962,47 +1053,42 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       }
       if (!ok) break;
       // ---------------------------------------------------------------- epilogue
-      const int bb = upper ? w.b1 : w.b0, hh = upper ? w.h1 : w.h0;
-      const int tok = 64 * w.j + r64;
+      float o[64];
+      if (nsteps > 0) {
+        // The same two-phase wait for the last PVs as in tile_roles.
+        if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
+        if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
+        tc_fence_after();
+        load_o_row(tcol + lane_base + 192, o);
+        tc_fence_before();
+        mbar_arrive(o_free);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; ++j) o[j] = 0.f;
+      }
+      const int grp = work_word(wk, 6), parts = work_word(wk, 5);
+      if (grp >= 0 && !split_finish(p, grp, parts >> 8, parts & 0xff, work_word(wk, 7), threadIdx.x & 127,
+                                    &bars->ep_bar[X], ep_phase, c.ep_flag + X, m, l, o, abort, ok)) {
+        if (!ok) break;
+        continue;   // another piece of this item merges the rows
+      }
+      const int u0 = work_word(wk, 0), u1r = work_word(wk, 1), u1 = u1r < 0 ? u0 : u1r;
+      PItem we;
+      we.b0 = u0 / a.H; we.h0 = u0 % a.H; we.b1 = u1 / a.H; we.h1 = u1 % a.H; we.j = wj;
+      const int bb = upper ? we.b1 : we.b0, hh = upper ? we.h1 : we.h0;
+      const int tok = 64 * we.j + r64;
       const bool valid = live && tok < a.S;
       const bool empty = valid && !(l > 0.f);
       uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + bb * a.os[0] +
                                                hh * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
-      if (nsteps > 0) {
-        // The same two-phase wait for the last PVs as in tc_fwd_kernel.
-        if (it >= 2 && !warp_mbar_wait(&o_done[(it - 2) & 1], ((it - 2) >> 1) & 1, abort)) { ok = false; break; }
-        if (!warp_mbar_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, abort)) { ok = false; break; }
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-        for (int hcol = 0; hcol < 2; ++hcol) {
-          uint32_t orow[32];
-          XSAKE_TMEM_LD32(tcol + lane_base + 192 + 32 * hcol, orow);
-          XSAKE_TMEM_WAIT_LD32(orow);
-          if (valid && !empty) {
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-              uint32_t wv[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                __nv_bfloat162 pb = __floats2bfloat162_rn(__uint_as_float(orow[8 * cc + 2 * q]) * inv,
-                                                          __uint_as_float(orow[8 * cc + 2 * q + 1]) * inv);
-                wv[q] = *reinterpret_cast<uint32_t*>(&pb);
-              }
-              orow_g[4 * hcol + cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-            }
-          }
-        }
-        tc_fence_before();
-        mbar_arrive(o_free);
-      }
+      if (valid && !empty) store_o_row(orow_g, o, 1.f / l);
       const bool empty_lo = __any_sync(0xffffffffu, empty && !upper);
       const bool empty_hi = __any_sync(0xffffffffu, empty && upper);
       if (empty_lo || empty_hi) {
         // Rows with no live score attend uniformly (the reference's finfo.min fill).
         float2 mean0 = make_float2(0.f, 0.f), mean1 = make_float2(0.f, 0.f);
-        if (empty_lo) warp_mean_v(a, w.b0, w.h0, mean0);
-        if (empty_hi) warp_mean_v(a, w.b1, w.h1, mean1);
+        if (empty_lo) warp_mean_v(a, we.b0, we.h0, mean0);
+        if (empty_hi) warp_mean_v(a, we.b1, we.h1, mean1);
 #pragma unroll
         for (int cc = 0; cc < 8; ++cc) {
           uint32_t wv[4];
@@ -1033,6 +1119,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   volatile int* abort = reinterpret_cast<volatile int*>(smem + kOffMisc + 4);
   volatile int* plan_ok = reinterpret_cast<volatile int*>(smem + kOffMisc + 8);
   volatile int* item_slots = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);   // [tile][slot]
+  volatile int* ep_flag = reinterpret_cast<volatile int*>(smem + kOffMisc + 48);      // [tile]
   const AttnArgs& a = p.a;
   const PlanLayout& L = a.L;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1049,6 +1136,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
         mbar_init(&bars->q_empty[t][s], 1);
       }
       mbar_init(&bars->o_free[s], 128);
+      mbar_init(&bars->ep_bar[s], 128);
       for (int b = 0; b < 2; ++b) mbar_init(&bars->o_done[s][b], 1);
       for (int b = 0; b < 3; ++b) mbar_init(&bars->p_full[s][b], 128);
       for (int b = 0; b < 3; ++b) mbar_init(&bars->s_full[s][b], 1);
@@ -1077,7 +1165,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   const uint32_t tmem = *tmem_slot;
 
   if (*plan_ok) {
-    const FwdCtx c{smem, bars, abort, item_slots, tmem, a.plan + L.f_rowptr_off, a.plan + L.f_entries_off};
+    const FwdCtx c{smem, bars, abort, item_slots, ep_flag, tmem, a.plan + L.f_entries_off};
     // The plan compiler chose the pairing from the mask (H_FWD_PAIR); every CTA reads the same word.
     if (a.plan[H_FWD_PAIR])
       pair_roles(tmQ, tmK, tmV, p, c);
@@ -1156,8 +1244,14 @@ bool tc_attn_fwd_supported(const AttnArgs& a, int dtype) {
   return ok;
 }
 
-// The work-item counter of the persistent scheduler.
-size_t tc_attn_fwd_workspace(const AttnArgs&) { return 256; }
+// Workspace: work-item counter (256 B) | split-group counters (kSplitSlots ints, reset with the
+// counter) | kSplitSlots partial slots of kSlotFloats floats.
+constexpr size_t kFwdGroupOff = 256;
+constexpr size_t kFwdResetBytes = kFwdGroupOff + 4 * kSplitSlots;
+constexpr size_t kFwdPartOff = (kFwdResetBytes + 255) / 256 * 256;
+constexpr size_t kFwdWsBytes = kFwdPartOff + (size_t)kSplitSlots * kSlotFloats * 4;
+
+size_t tc_attn_fwd_workspace() { return kFwdWsBytes; }
 
 int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   DeviceInfo di;
@@ -1165,8 +1259,9 @@ int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (st) return st;
   XSAKE_REQUIRE(di.major == 10, XSAKE_EUNSUPPORTED, "tensor-core path needs sm_100 (got sm_%d%d)", di.major,
                 di.minor);
-  XSAKE_REQUIRE(ws != nullptr && ws_bytes >= 256 && ((uintptr_t)ws & 15) == 0, XSAKE_EINVAL,
-                "the tensor-core forward needs a 256-byte, 16-byte aligned workspace (got %zu bytes)", ws_bytes);
+  XSAKE_REQUIRE(ws != nullptr && ws_bytes >= kFwdWsBytes && ((uintptr_t)ws & 255) == 0, XSAKE_EINVAL,
+                "the tensor-core forward needs a %zu-byte, 256-byte aligned workspace (got %zu bytes)", kFwdWsBytes,
+                ws_bytes);
   // The plan (H_FWD_PAIR) chooses the pairing on the device; the grid covers either item count.
   CUtensorMap mq, mk, mv;
   if ((st = tc_make_map(&mq, a.q, a.qs, a.B, a.H, a.S, 64))) return st;
@@ -1184,9 +1279,11 @@ int tc_attn_fwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   p.a = a;
   p.scale_log2 = a.scale * kLog2e;
   p.counter = reinterpret_cast<int*>(ws);
-  XSAKE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(int), s));
-  const int items = std::max(a.L.nitems, pair_items(a.L, a.B, a.H));
-  const int grid = std::max(1, std::min((items + 1) / 2, di.sm_count));
+  p.grp_counter = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) + kFwdGroupOff);
+  p.parts = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kFwdPartOff);
+  XSAKE_CUDA_TRY(cudaMemsetAsync(ws, 0, kFwdResetBytes, s));
+  // Work items: at most the plan's table size (the count itself is on the device).
+  const int grid = std::max(1, std::min((a.L.max_work + 1) / 2, di.sm_count));
   tc_fwd_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, p);
   return check_launch("tc_fwd_kernel");
 }

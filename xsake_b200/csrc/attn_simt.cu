@@ -75,6 +75,7 @@ __global__ void __launch_bounds__(128) simt_fwd_kernel(AttnArgs a) {
   __syncthreads();
   if (!s_ok) return;
   const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  if (!plan_unit_selected(a.plan, a.L, b, h)) return;   // a unit this plan does not compute
   const int q0 = blockIdx.x * kQT, q1 = min(q0 + kQT, a.S) - 1;
   const int r = threadIdx.x >> 1, hf = threadIdx.x & 1;
   const int row = q0 + r;
@@ -145,6 +146,7 @@ __global__ void __launch_bounds__(128) simt_fwd_kernel(AttnArgs a) {
 template <typename T>
 __global__ void __launch_bounds__(256) bwd_prep_kernel(AttnArgs a) {
   const int bh = blockIdx.x, b = bh / a.H, h = bh % a.H;
+  if (!plan_unit_selected(a.plan, a.L, b, h)) return;   // a unit this plan does not compute
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5;
   for (int row = warp; row < a.S; row += nw) {
@@ -180,6 +182,7 @@ __global__ void __launch_bounds__(128) simt_dq_kernel(AttnArgs a) {
   __syncthreads();
   if (!s_ok) return;
   const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  if (!plan_unit_selected(a.plan, a.L, b, h)) return;   // a unit this plan does not compute
   const int q0 = blockIdx.x * kQT, q1 = min(q0 + kQT, a.S) - 1;
   const int r = threadIdx.x >> 1, hf = threadIdx.x & 1;
   const int row = q0 + r;
@@ -241,6 +244,7 @@ __global__ void __launch_bounds__(128) simt_dkdv_kernel(AttnArgs a) {
   __syncthreads();
   if (!s_ok) return;
   const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
+  if (!plan_unit_selected(a.plan, a.L, b, h)) return;   // a unit this plan does not compute
   const int k0 = blockIdx.x * kQT, k1 = min(k0 + kQT, a.S) - 1;
   const int r = threadIdx.x >> 1, hf = threadIdx.x & 1;
   const int key = k0 + r;

@@ -33,11 +33,17 @@ from . import _lib
 
 # ----------------------------------------------------------------------------- mask plans
 class CompiledMask:
-    """A block mask compiled for one (batch, heads, seq, block_size, causal) problem."""
+    """A block mask compiled for one (batch, heads, seq, block_size, causal) problem.
 
-    def __init__(self, plan: torch.Tensor, dims: _lib.MaskDims):
+    ``units`` (a sorted tuple of unit ids ``b * heads + h``, or None for every unit) are the
+    (batch, head) units the attention calls with this plan compute: a rank of a job whose
+    batch x heads is sharded over GPUs compiles a plan of its own units, and the kernels then
+    read and write only those units' rows."""
+
+    def __init__(self, plan: torch.Tensor, dims: _lib.MaskDims, units=None):
         self.plan = plan
         self.dims = dims
+        self.units = units
         self._stats = None
 
     @property
@@ -61,13 +67,19 @@ class CompiledMask:
         return bool(self.dims.causal)
 
     def stats(self) -> dict:
-        """Active block pairs after the causal cut (n_a), computed 64x64 tiles, fully masked
-        q-blocks and forward work items.  Synchronises the current stream."""
+        """Active block pairs after the causal cut (n_a) of the selected units, 64x64 tiles the
+        forward computes with the pairing the plan chose, fully masked q-blocks, forward work
+        items, and the plan compiler's choices (pairing, split pieces).  Synchronises the
+        current stream."""
         if self._stats is None:
-            out = (C.c_int64 * 4)()
-            _lib.check(_lib.load().xsake_mask_plan_stats(self.plan.data_ptr(), dev.stream_ptr(), out))
-            self._stats = {"active_blocks": out[0], "computed_tiles": out[1],
-                           "empty_qblocks": out[2], "work_items": out[3]}
+            info = _lib.PlanInfo()
+            _lib.check(_lib.load().xsake_mask_plan_info(self.plan.data_ptr(), dev.stream_ptr(), C.byref(info)))
+            self._stats = {"active_blocks": info.active_blocks, "computed_tiles": info.computed_tiles,
+                           "empty_qblocks": info.empty_qblocks, "work_items": info.work_items,
+                           "selected_units": info.selected_units,
+                           "pairing": "unit" if info.unit_pairing else "query_chunk",
+                           "split_items": info.split_items, "split_slots": info.split_slots,
+                           "split_cap": info.split_cap, "workers": info.workers}
         return self._stats
 
 
@@ -86,13 +98,39 @@ def _mask_4d(block_mask):
     return m
 
 
-def _mask_key(m) -> bytes:
+# Recently seen host masks by object identity: (bool snapshot, digest).  A hit still compares
+# the whole content (a mask may have been written in place), which is cheaper than hashing it.
+_SEEN: "OrderedDict[int, tuple]" = OrderedDict()
+_SEEN_MAX = 8
+
+
+def _mask_key(m, ident: int) -> bytes:
+    """Content key of a block mask (``ident``: id of the caller's object).  A CUDA mask is copied
+    to the host (nq * nk bytes per mask head; this synchronises its stream), so a plan is never
+    matched by a tensor's address, which the caching allocator reuses."""
     if isinstance(m, torch.Tensor):
-        if m.is_cuda:
-            return b"cuda" + repr((m.data_ptr(), m._version, tuple(m.shape), m.dtype)).encode()
-        m = m.numpy()
+        m = m.detach().cpu().numpy()
     a = np.ascontiguousarray(np.asarray(m).astype(bool, copy=False))
-    return hashlib.blake2b(a.tobytes() + repr(a.shape).encode(), digest_size=16).digest()
+    seen = _SEEN.get(ident)
+    if seen is not None and seen[0].shape == a.shape and np.array_equal(seen[0], a):
+        _SEEN.move_to_end(ident)
+        return seen[1]
+    key = hashlib.blake2b(a.tobytes() + repr(a.shape).encode(), digest_size=16).digest()
+    _SEEN[ident] = (a.copy(), key)
+    if len(_SEEN) > _SEEN_MAX:
+        _SEEN.popitem(last=False)
+    return key
+
+
+def _units_tuple(units, batch: int, heads: int):
+    if units is None:
+        return None
+    u = sorted({int(x) for x in np.asarray(units).reshape(-1)})
+    if not u:
+        raise ValueError("units must name at least one (batch, head) unit")
+    if u[0] < 0 or u[-1] >= batch * heads:
+        raise ValueError(f"unit ids must lie in [0, batch * heads = {batch * heads})")
+    return None if len(u) == batch * heads else tuple(u)
 
 
 _CACHE: "OrderedDict[tuple, CompiledMask]" = OrderedDict()
@@ -100,9 +138,14 @@ _CACHE_MAX = 32
 
 
 def compile_block_mask(block_mask, batch: int, heads: int, seq: int, block_size: int,
-                       causal: bool, device=None) -> CompiledMask:
-    """Compile ``block_mask`` (broadcast like ``_broadcast_mask``) into a device plan."""
+                       causal: bool, device=None, units=None, workers: int = 0) -> CompiledMask:
+    """Compile ``block_mask`` (broadcast like ``_broadcast_mask``) into a device plan.
+
+    ``units`` (unit ids ``b * heads + h``; None = all) restricts the plan to those (batch,
+    head) units.  ``workers`` (0 = two per SM of the device) is the concurrency the forward's
+    split rule assumes."""
     dev.require_cuda()
+    units = _units_tuple(units, batch, heads)
     if isinstance(block_mask, CompiledMask):
         cm = block_mask
         if (cm.batch, cm.heads, cm.seq, cm.block_size, cm.causal) != (batch, heads, seq, block_size,
@@ -110,6 +153,8 @@ def compile_block_mask(block_mask, batch: int, heads: int, seq: int, block_size:
             raise ValueError(f"CompiledMask was built for (batch, heads, seq, block_size, causal) = "
                              f"{(cm.batch, cm.heads, cm.seq, cm.block_size, cm.causal)}, called with "
                              f"{(batch, heads, seq, block_size, bool(causal))}")
+        if units is not None and cm.units != units:
+            raise ValueError("CompiledMask was built for other units")
         return cm
     if block_size <= 0 or seq % block_size:
         raise ValueError(f"block_size {block_size} must divide seq {seq}")
@@ -122,7 +167,8 @@ def compile_block_mask(block_mask, batch: int, heads: int, seq: int, block_size:
     if Bm not in (1, batch) or Hm not in (1, heads):
         raise ValueError(f"block_mask leading dims {(Bm, Hm)} do not broadcast to {(batch, heads)}")
     device = device or torch.device("cuda", torch.cuda.current_device())
-    key = (_mask_key(m), batch, heads, seq, block_size, bool(causal), str(device))
+    key = (_mask_key(m, id(block_mask)), batch, heads, seq, block_size, bool(causal), str(device), units,
+           int(workers))
     hit = _CACHE.get(key)
     if hit is not None:
         _CACHE.move_to_end(key)
@@ -135,10 +181,15 @@ def compile_block_mask(block_mask, batch: int, heads: int, seq: int, block_size:
     mt = mt.to(device=device, dtype=torch.uint8).contiguous() if mt.dtype != torch.uint8 else \
         mt.to(device).contiguous()
     plan = torch.empty(nbytes.value, dtype=torch.uint8, device=device)
-    _lib.check(lib.xsake_mask_compile(C.byref(dims), mt.data_ptr(), plan.data_ptr(), nbytes.value,
-                                      dev.stream_ptr()))
-    cm = CompiledMask(plan, dims)
-    cm._mask_ref = mt  # keep the source alive until the compile kernels have run
+    ut = None
+    if units is not None:
+        ut = torch.tensor(units, dtype=torch.int32).to(device)
+    opts = _lib.PlanOptions(ut.data_ptr() if ut is not None else None, len(units) if units else 0,
+                            int(workers))
+    _lib.check(lib.xsake_mask_compile_ex(C.byref(dims), C.byref(opts), mt.data_ptr(), plan.data_ptr(),
+                                         nbytes.value, dev.stream_ptr()))
+    cm = CompiledMask(plan, dims, units)
+    cm._mask_ref = (mt, ut)  # keep the sources alive until the compile kernels have run
     _CACHE[key] = cm
     if len(_CACHE) > _CACHE_MAX:
         _CACHE.popitem(last=False)
@@ -275,6 +326,56 @@ def sparse_attention_pallas(q, k, v, block_mask, block_q: int = 128, block_k: in
     else:
         out, _ = attention_forward(q, k, v, block_mask, block_q, sm_scale, causal)
     return _finish(out, was_host)
+
+
+def sparse_attention_shard(q, k, v, block_mask, units, block_size: int = 128, sm_scale: Optional[float] = None,
+                           causal: bool = False, out=None, buffers=None):
+    """Forward of the (batch, head) units ``units`` (ids ``b * heads + h``) of one job: the share
+    of a rank when the job's batch x heads is split over GPUs (the reference runs a job on one
+    device, sparse_attention.py:161-252; units are independent, so the split needs no exchange).
+
+    ``q``, ``k``, ``v`` are the job's ``[B, H, S, D]`` tensors.  CUDA tensors are used in place and
+    the result is a CUDA tensor whose rows of other units are unspecified.  Host tensors (torch
+    CPU tensors, pinned for asynchronous copies, or NumPy arrays) have only the listed units'
+    ``[S, D]`` slices copied to the device and the output slices copied back into ``out`` (a host
+    tensor of q's shape and dtype, allocated when None; other units' rows are left as they are),
+    stream-ordered on the current stream.  ``buffers`` (q, k, v, o device tensors of the job's
+    shape) may be passed to reuse device memory across calls."""
+    was_host = not (isinstance(q, torch.Tensor) and q.is_cuda)
+    if not was_host:
+        B, H, S, _ = q.shape
+        cm = compile_block_mask(block_mask, B, H, S, block_size, causal, q.device, units=units)
+        return attention_forward(q, k, v, cm, block_size, sm_scale, causal)[0]
+    dev.require_cuda()
+    ht = [x if isinstance(x, torch.Tensor) else dev.host_tensor(x) for x in (q, k, v)]
+    if ht[0].dim() != 4 or any(t.shape != ht[0].shape or t.dtype != ht[0].dtype for t in ht):
+        raise ValueError("q, k, v must be [batch, heads, seq, d_head] of one shape and dtype")
+    B, H, S, D = ht[0].shape
+    device = torch.device("cuda", torch.cuda.current_device())
+    cm = compile_block_mask(block_mask, B, H, S, block_size, causal, device, units=units)
+    sel = cm.units if cm.units is not None else tuple(range(B * H))
+    if buffers is None:
+        buffers = tuple(torch.empty(ht[0].shape, dtype=ht[0].dtype, device=device) for _ in range(4))
+    qd, kd, vd, od = buffers
+    # one copy per run of consecutive unit ids (a run is contiguous [S, D] slices of [B*H, S, D])
+    runs, start = [], sel[0]
+    for a, b in zip(sel, sel[1:] + (None,)):
+        if b != a + 1:
+            runs.append((start, a + 1))
+            start = b
+    flat = lambda t: t.contiguous().view(B * H, S, D)   # noqa: E731
+    hq, hk, hv = (flat(t) for t in ht)
+    fq, fk, fv = (t.view(B * H, S, D) for t in (qd, kd, vd))
+    for lo, hi in runs:
+        for d_, h_ in ((fq, hq), (fk, hk), (fv, hv)):
+            d_[lo:hi].copy_(h_[lo:hi], non_blocking=True)
+    o, _ = attention_forward(qd, kd, vd, cm, block_size, sm_scale, causal)
+    if out is None:
+        out = torch.empty(ht[0].shape, dtype=ht[0].dtype, pin_memory=True)
+    fo, ho = o.view(B * H, S, D), out.view(B * H, S, D)
+    for lo, hi in runs:
+        ho[lo:hi].copy_(fo[lo:hi], non_blocking=True)
+    return out
 
 
 def attention_probabilities(q, k, block_mask, block_size: int = 128, scale: Optional[float] = None,
