@@ -158,6 +158,16 @@ XSAKE_API int xsake_attn_bwd(const XsakeAttnDesc* desc, const void* plan_dev, co
 XSAKE_API int xsake_attn_probs(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
                    const void* k_dev, float* p_dev, void* stream);
 
+/* compute_attention_entropy (kernels/hads/hads_pattern.py:36-50) of exactly the weights
+ * xsake_attn_probs gives (masked by the plan, causal cut, finfo.min fill), without materialising
+ * them: head_sums_dev[h] (fp64) = sum over (b, q) of -sum_k c log c, c = clip(p, 1e-9, 1).  This is
+ * what the reference's calibration reduces (the layer-0 weights of training/trainer.py:79-117).
+ * Strided q, k as in desc; the workspace is xsake_entropy_qk_workspace_size(batch, heads, seq)
+ * bytes.  Deterministic. */
+XSAKE_API int xsake_attn_entropy(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
+                   const void* k_dev, double* head_sums_dev, void* workspace_dev, size_t workspace_bytes,
+                   void* stream);
+
 /* ------------------------------------------------------------------ row kernels
  * fused_softmax / fused_softmax_pallas / _softmax_kernel
  * (kernels/pallas/fused_softmax.py:26-87): softmax over the last axis of a contiguous
@@ -240,9 +250,20 @@ XSAKE_API int xsake_entropy_rows_noalloc(const float* p_dev, int64_t batch, int6
  * Rank 0 calls xsake_comm_unique_id and hands the 128 bytes to every rank out of band; each
  * rank then calls xsake_comm_init with the CUDA device it will use current. */
 XSAKE_API int xsake_comm_unique_id(uint8_t id_out[128]);
+/* xsake_comm_init_ex with a 300 s bound. */
 XSAKE_API int xsake_comm_init(const uint8_t id[128], int nranks, int rank, void** comm_out);
-/* In place on buf_dev (count doubles), stream-ordered on `stream`. */
+/* Failure handling (the reference has none on this path): the communicator is non-blocking and
+ * every host-side wait of this rank is bounded by timeout_ms (<= 0: unbounded).  A rank that
+ * never joins makes init return XSAKE_ETIMEOUT after timeout_ms, with the communicator aborted;
+ * the process and its GPU stay usable. */
+XSAKE_API int xsake_comm_init_ex(const uint8_t id[128], int nranks, int rank, int timeout_ms, void** comm_out);
+/* In place on buf_dev (count doubles), stream-ordered on `stream`; returns once the collective is
+ * enqueued (bounded by the communicator's timeout). */
 XSAKE_API int xsake_comm_allreduce_sum_f64(void* comm, double* buf_dev, size_t count, void* stream);
+/* Waits on the host, at most timeout_ms, until `stream` has finished the collectives enqueued on
+ * it.  A peer that died or never entered the collective: the communicator is aborted (which ends
+ * its kernels still waiting on the stream) and XSAKE_ETIMEOUT returned; destroy it afterwards. */
+XSAKE_API int xsake_comm_wait(void* comm, void* stream, int timeout_ms);
 XSAKE_API int xsake_comm_destroy(void* comm);
 
 #ifdef __cplusplus

@@ -115,3 +115,61 @@ def test_entropy_qk_rejects_bad_arguments():
         hp.entropy_head_sums_qk(q, torch.zeros(1, 2, 32, 64, device="cuda"))
     with pytest.raises(Exception):
         hp.entropy_head_sums_qk(torch.zeros(1, 2, 64, 48, device="cuda"), torch.zeros(1, 2, 64, 48, device="cuda"))
+
+
+@pytest.mark.parametrize("dtype,layout", [("f32", "bhsd"), ("bf16", "bshd")])
+def test_masked_entropy_matches_weights_entropy(dtype, layout):
+    """xsake_attn_entropy: the entropy of the masked causal weights (what the reference's
+    calibration reduces) without materialising them, against the oracle's weights, 1e-5 relative;
+    a fully masked q-block (uniform rows) included; [B, S, H, D] memory read through strides."""
+    from xsake_b200 import hads_pattern as hp
+    B, H, S, D, bs = 2, 3, 512, 64, 64
+    m = oh.dummy_hads_profile(H, S, bs, causal=True, global_blocks=1).block_masks.copy()
+    m[2, 3, :] = False
+    q, k = _rand((B, H, S, D), 600), _rand((B, H, S, D), 601)
+    q *= np.linspace(0.5, 3, H, dtype=np.float32)[None, :, None, None]
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    if dtype == "bf16":
+        q, k = (oi.to_bf16(x).astype(np.float32) for x in (q, k))
+    tq, tk = (torch.from_numpy(x).to(tdt).cuda() for x in (q, k))
+    if layout == "bshd":
+        tq, tk = (t.transpose(1, 2).contiguous().transpose(1, 2) for t in (tq, tk))
+    sums = hp.entropy_head_sums_attention(tq, tk, m, bs, None, causal=True).cpu().numpy()
+    _, ref_p = oa.sparse_attention_reference(q, k, k, m, bs, causal=True)
+    ref = oh.entropy_head_sums(ref_p)
+    assert np.max(np.abs(sums - ref) / np.abs(ref)) <= ENT_RTOL
+
+
+def test_model_calibration_and_recalibration_step():
+    """trainer.calibrate_hads (training/trainer.py:79-117): the first layer's masked causal
+    weights over n_steps batches, reduced by the fused kernel, give the profile the reference's
+    path builds from the materialised weights (entropies 1e-5 relative; masks bit-exact on heads
+    whose keep margin is at least 1e-4); maybe_recalibrate attaches it at the multiples of
+    `every` only."""
+    from xsake_b200 import hads_pattern as hp
+    from xsake_b200 import sparse_attention as sa
+    from xsake_b200 import trainer
+    from xsake_b200.model import ModelConfig, XSAKETransformer
+    cfg = ModelConfig(vocab_size=512, seq_len=512, n_layers=2, n_heads=4, d_model=256, d_ff=512,
+                      block_size=64, dtype="float32", calibration_steps=3)
+    torch.manual_seed(0)
+    model = XSAKETransformer(cfg, device="cuda")
+    batches = [torch.randint(0, 512, (2, 512), device="cuda") for _ in range(3)]
+    prof = trainer.calibrate_hads(model, iter(batches), cfg)
+    per_step = []
+    for ids in batches:
+        q, k, mask, bs, scale = model.layer0_qk(ids)
+        p = sa.attention_probabilities(q.float(), k.float(), mask, bs, scale, True).cpu().numpy()
+        per_step.append(oh.compute_attention_entropy(p))
+    ent_ref = np.mean(per_step, axis=0)
+    assert np.max(np.abs(prof.head_entropies - ent_ref) / np.abs(ent_ref)) <= ENT_RTOL
+    ref = oh.profile_from_entropies(ent_ref.astype(np.float32), 512, 64, causal=True)
+    for h in range(4):
+        if oh.keep_margin(ref.head_sparsity[h], 8) >= 1e-4:
+            np.testing.assert_array_equal(prof.block_masks[h], ref.block_masks[h], err_msg=f"head {h}")
+    assert trainer.maybe_recalibrate(5, 10, model, iter(batches), cfg) is None
+    assert model.blocks[1].attn.hads_profile is None
+    new = trainer.maybe_recalibrate(10, 10, model, iter(batches), cfg)
+    assert new is not None and all(b.attn.hads_profile is new for b in model.blocks)
+    np.testing.assert_array_equal(new.block_masks, prof.block_masks)
+    assert hp.profile_summary(new)["n_heads"] == 4

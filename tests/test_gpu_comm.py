@@ -85,3 +85,23 @@ def test_two_rank_calibration_exchange(tmp_path):
     ref = oh.build_hads_profile([_batch(i).cpu().numpy() for i in range(5)], S, 64, causal=True, global_blocks=1)
     np.testing.assert_allclose(r0["ent"], ref.head_entropies, rtol=1e-5)
     np.testing.assert_array_equal(r0["mask"], ref.block_masks)
+
+
+def test_rank_that_never_joins_times_out():
+    """A two-rank communicator whose second rank never calls init: rank 0's init returns
+    XSAKE_ETIMEOUT within its deadline (bootstrap only, no collective in flight), the
+    communicator is aborted, and the process goes on to use a new communicator."""
+    import time
+    from xsake_b200 import _lib, comm
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    uid = comm.unique_id()
+    t0 = time.monotonic()
+    with pytest.raises(_lib.XsakeError) as e:
+        comm.Comm(uid, 2, 0, device=0, timeout_s=2.0)
+    assert e.value.code == _lib.XSAKE_ETIMEOUT
+    assert time.monotonic() - t0 < 30.0
+    with comm.Comm(comm.unique_id(), 1, 0, device=0, timeout_s=30.0) as c:
+        t = torch.ones(12, dtype=torch.float64, device="cuda")
+        c.allreduce_sum_f64(t)
+        c.wait(10.0)
+        assert torch.equal(t, torch.ones_like(t))

@@ -78,3 +78,20 @@ def test_lpt_shard_balances_hads_units():
         loads = [costs[p].sum() for p in parts]
         assert max(loads) <= 1.05 * costs.sum() / world + costs.max()
         assert parts == cal.lpt_shard(costs, world)            # deterministic
+
+
+def test_pair_shard_keeps_unit_pairs_and_balances():
+    from xsake_b200 import calibration as cal
+    masks = oh.dummy_hads_profile(12, 4096, 64, causal=True, global_blocks=1).block_masks
+    costs = cal.unit_costs(masks, batch=4)
+    for world in (1, 2, 4, 8):
+        parts = cal.pair_shard(masks, 4, world)
+        assert sorted(u for p in parts for u in p) == list(range(48))
+        for p in parts:                     # batch units (0, 1) and (2, 3) of a head stay together
+            for u in p:
+                b, h = divmod(u, 12)
+                assert (b ^ 1) * 12 + h in p
+        loads = [costs[p].sum() for p in parts]
+        assert max(loads) <= 1.1 * costs.sum() / world
+    odd = cal.pair_shard(masks, 3, 2)       # odd batch: the last batch unit of a head runs alone
+    assert sorted(u for p in odd for u in p) == list(range(36))

@@ -40,20 +40,52 @@ def _cached_mask(key, build):
     return m
 
 
+def _config_fields(cfg):
+    """The layer's fields from a model config: the reference's ModelConfig with a nested
+    ``kernel`` (model/config.py:18-58) or this package's flat ModelConfig."""
+    k = getattr(cfg, "kernel", None)
+    hads = getattr(k, "hads", None) if k is not None else None
+    pick = lambda obj, name, flat: getattr(obj, name) if obj is not None else getattr(cfg, flat)   # noqa: E731
+    dtype = torch.bfloat16 if getattr(cfg, "dtype", "bfloat16") == "bfloat16" else torch.float32
+    return dict(d_model=cfg.d_model, n_heads=cfg.n_heads, n_layers=cfg.n_layers, bias=cfg.bias,
+                dropout=cfg.dropout, dtype=dtype, block_size=pick(k, "block_size_q", "block_size"),
+                sparsity_type=pick(k, "sparsity_type", "sparsity_type"),
+                min_sparsity=pick(hads, "min_sparsity", "min_sparsity"),
+                max_sparsity=pick(hads, "max_sparsity", "max_sparsity"),
+                window_size=pick(hads, "window_size", "window_size"))
+
+
 class XSAKEAttention(nn.Module):
     """Drop-in for model/attention.py's XSAKEAttention.
 
-    Args mirror the reference's ModelConfig fields the layer reads: d_model, n_heads, n_layers
-    (output-projection init scale), bias, dropout, dtype, and the kernel config: block_size
-    (``block_size_q``), sparsity_type, and the HADS parameters used for the uncalibrated profile.
-    """
+    Constructed like the reference, ``XSAKEAttention(config, hads_profile=None)``
+    (model/attention.py:41-42, ``config`` a ModelConfig), or from the fields the layer reads:
+    d_model, n_heads, n_layers (output-projection init scale), bias, dropout, dtype, and the
+    kernel config: block_size (``block_size_q``), sparsity_type, and the HADS parameters used
+    for the uncalibrated profile.  Keywords given next to a config override its fields (e.g.
+    ``dtype=torch.float32`` for fp32 master weights under autocast)."""
 
-    def __init__(self, d_model: int, n_heads: int, n_layers: int = 12, bias: bool = False,
-                 dropout: float = 0.0, dtype=torch.bfloat16, block_size: int = 128,
+    def __init__(self, d_model=None, n_heads=None, n_layers: int = 12, bias: bool = False,
+                 dropout: float = 0.0, dtype=None, block_size: int = 128,
                  sparsity_type: str = "hads", hads_profile: Optional[hp.HADSProfile] = None,
                  min_sparsity: float = 0.10, max_sparsity: float = 0.90, window_size: int = 2,
-                 device=None):
+                 device=None, config=None):
+        if config is None and d_model is not None and not isinstance(d_model, int):
+            config, d_model = d_model, None
+        if config is not None:
+            if n_heads is not None and not isinstance(n_heads, int):    # XSAKEAttention(config, profile)
+                hads_profile, n_heads = n_heads, None
+            f = _config_fields(config)
+            d_model, n_heads, n_layers, bias, dropout = (f["d_model"], f["n_heads"], f["n_layers"], f["bias"],
+                                                         f["dropout"])
+            dtype = dtype if dtype is not None else f["dtype"]
+            block_size, sparsity_type = f["block_size"], f["sparsity_type"]
+            min_sparsity, max_sparsity, window_size = f["min_sparsity"], f["max_sparsity"], f["window_size"]
+        if d_model is None or n_heads is None:
+            raise TypeError("XSAKEAttention needs a model config or d_model and n_heads")
+        dtype = dtype if dtype is not None else torch.bfloat16
         super().__init__()
+        self.config = config
         if d_model % n_heads:
             raise ValueError("d_model must be a multiple of n_heads")
         self.d_model, self.n_heads, self.d_head = d_model, n_heads, d_model // n_heads
@@ -72,6 +104,11 @@ class XSAKEAttention(nn.Module):
                 if lin.bias is not None:
                     nn.init.zeros_(lin.bias)
         self.drop = nn.Dropout(dropout)
+
+    @classmethod
+    def from_config(cls, config, hads_profile: Optional[hp.HADSProfile] = None, **overrides):
+        """``XSAKEAttention(config, hads_profile)`` of model/attention.py:41-42."""
+        return cls(config=config, hads_profile=hads_profile, **overrides)
 
     def _heads(self, t: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
         # [B, S, d_model] -> [B, H, S, D] view of the same memory (strides S*H*D, D, H*D, 1)

@@ -33,28 +33,28 @@ def _dist():
     return dist if (dist.is_available() and dist.is_initialized()) else None
 
 
-def calibrate(batch_attn: Callable[[int], torch.Tensor], n_batches: int, seq_len: int, block_size: int,
-              min_sparsity: float = 0.10, max_sparsity: float = 0.90, window_size: int = 2,
-              causal: bool = True, global_blocks: int = 0,
-              head_sums: Callable[[torch.Tensor], torch.Tensor] = hp.entropy_head_sums,
-              group: Optional[object] = None, device=None, comm=None) -> hp.HADSProfile:
-    """Build a HADS profile from ``n_batches`` calibration batches split over the ranks of
-    ``group`` (or a single process).  ``batch_attn(i)`` returns the attention weights
-    [B, H, Sq, Sk] of batch i; ``head_sums`` reduces them to float64 per-head entropy sums.
-    With ``comm`` (an ``xsake_b200.comm.Comm``) the exchange runs through the library's NCCL
-    entry points instead of torch.distributed."""
-    dist = _dist()
+def _world(group=None, comm=None):
     if comm is not None:
-        world, rank = comm.nranks, comm.rank
-    else:
-        world = dist.get_world_size(group) if dist else 1
-        rank = dist.get_rank(group) if dist else 0
+        return comm.nranks, comm.rank
+    dist = _dist()
+    return (dist.get_world_size(group), dist.get_rank(group)) if dist else (1, 0)
+
+
+def calibrate_sums(batch_sums: Callable[[int], tuple], n_batches: int, seq_len: int, block_size: int,
+                   min_sparsity: float = 0.10, max_sparsity: float = 0.90, window_size: int = 2,
+                   causal: bool = True, global_blocks: int = 0, group: Optional[object] = None, device=None,
+                   comm=None) -> hp.HADSProfile:
+    """Build a HADS profile from ``n_batches`` calibration batches split round-robin over the
+    ranks of ``group`` (or ``comm``, or one process).  ``batch_sums(i)`` returns batch i's float64
+    per-head entropy sums over its rows and the row count; the sums and counts are summed over
+    ranks (one fp64 all-reduce each) and every rank builds the same masks."""
+    world, rank = _world(group, comm)
     sums, rows = None, 0
     for i in local_batches(n_batches, world, rank):
-        p = batch_attn(i)
-        s = head_sums(p).to(torch.float64)
+        s, r = batch_sums(i)
+        s = s.to(torch.float64)
         sums = s if sums is None else sums + s
-        rows += int(p.shape[0]) * int(p.shape[2])
+        rows += int(r)
     if sums is None:
         raise ValueError("every rank needs at least one calibration batch")
     if device is not None:
@@ -68,6 +68,22 @@ def calibrate(batch_attn: Callable[[int], torch.Tensor], n_batches: int, seq_len
     ent = (sums / total).to(torch.float32).cpu().numpy()
     return hp.profile_from_entropies(ent, seq_len, block_size, min_sparsity, max_sparsity, window_size,
                                      causal, global_blocks)
+
+
+def calibrate(batch_attn: Callable[[int], torch.Tensor], n_batches: int, seq_len: int, block_size: int,
+              min_sparsity: float = 0.10, max_sparsity: float = 0.90, window_size: int = 2,
+              causal: bool = True, global_blocks: int = 0,
+              head_sums: Callable[[torch.Tensor], torch.Tensor] = hp.entropy_head_sums,
+              group: Optional[object] = None, device=None, comm=None) -> hp.HADSProfile:
+    """``calibrate_sums`` for callers that hold the attention weights: ``batch_attn(i)`` returns
+    the weights [B, H, Sq, Sk] of batch i and ``head_sums`` reduces them to float64 per-head
+    entropy sums.  With ``comm`` (an ``xsake_b200.comm.Comm``) the exchange runs through the
+    library's NCCL entry points instead of torch.distributed."""
+    def batch_sums(i):
+        p = batch_attn(i)
+        return head_sums(p), int(p.shape[0]) * int(p.shape[2])
+    return calibrate_sums(batch_sums, n_batches, seq_len, block_size, min_sparsity, max_sparsity, window_size,
+                          causal, global_blocks, group, device, comm)
 
 
 def unit_costs(block_masks: np.ndarray, batch: int, causal: bool = True) -> np.ndarray:

@@ -26,19 +26,30 @@ def unique_id() -> bytes:
 
 
 class Comm:
-    """One rank of an NCCL communicator over ``nranks`` processes (one GPU each)."""
+    """One rank of an NCCL communicator over ``nranks`` processes (one GPU each).
 
-    def __init__(self, uid: bytes, nranks: int, rank: int, device=None):
+    Every host-side wait of this rank is bounded by ``timeout_s`` (None: unbounded): a rank that
+    never joins makes the constructor raise ``XsakeError`` with code ``XSAKE_ETIMEOUT`` after that
+    long (the communicator is aborted; the process and its GPU stay usable), and ``wait`` does the
+    same for a collective a peer never entered."""
+
+    def __init__(self, uid: bytes, nranks: int, rank: int, device=None, timeout_s: float = 300.0):
         if len(uid) != 128:
             raise ValueError("the NCCL unique id has 128 bytes")
-        dev.require_cuda()
         if device is not None:
+            dev.require_cuda()
             torch.cuda.set_device(device)
         self._lib = _lib.load()
         self._uid = (C.c_uint8 * 128).from_buffer_copy(uid)
         self._comm = C.c_void_p()
-        _lib.check(self._lib.xsake_comm_init(self._uid, nranks, rank, C.byref(self._comm)))
+        self.timeout_ms = 0 if timeout_s is None else max(1, int(timeout_s * 1000))
+        _lib.check(self._lib.xsake_comm_init_ex(self._uid, nranks, rank, self.timeout_ms, C.byref(self._comm)))
         self.nranks, self.rank = nranks, rank
+
+    def wait(self, timeout_s: float = None) -> None:
+        """Block (bounded) until the current stream has finished the collectives on it."""
+        ms = self.timeout_ms if timeout_s is None else max(1, int(timeout_s * 1000))
+        _lib.check(self._lib.xsake_comm_wait(self._comm, dev.stream_ptr(), ms))
 
     def allreduce_sum_f64(self, t: torch.Tensor) -> torch.Tensor:
         """In-place sum over ranks of a contiguous float64 CUDA tensor (stream-ordered)."""

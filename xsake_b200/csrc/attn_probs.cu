@@ -8,6 +8,9 @@
 //   entropy  compute_attention_entropy (kernels/hads/hads_pattern.py:36-50) of softmax(Q K^T *
 //            scale) without materialising P: per row H = -sum_k c log c, c = clip(p, 1e-9, 1),
 //            summed per head in fp64 in a fixed order (per-CTA partials, then one pass per head).
+//   masked entropy  the same of the masked weights `probs` gives (the weights the reference's
+//            calibration collects from layer 0, training/trainer.py:79-117): masked keys have
+//            p = 0 and so contribute the clipped 1e-9 term, as in the reference.
 //
 // Scores are fp32 products (TF32 would move entropies by ~1e-3).  CTA = 256 threads on a tile of
 // 64 query rows of one (b, h); K arrives in 64-key tiles staged transposed in shared memory;
@@ -55,13 +58,18 @@ __device__ __forceinline__ float rescale_sum(float l, float m, float mn) {
   return (m == -INFINITY) ? 0.f : l * __expf(m - mn);
 }
 
-template <typename T, int D, bool PROBS>
+// MODE: kEntropy (no mask), kProbs (masked weights), kMaskedEntropy (entropy of the masked weights)
+constexpr int kEntropy = 0, kProbs = 1, kMaskedEntropy = 2;
+
+template <typename T, int D, int MODE>
 __global__ void __launch_bounds__(kThreadsP) probs_kernel(ProbsArgs a) {
+  constexpr bool PROBS = MODE == kProbs;
+  constexpr bool MASKED = MODE != kEntropy;
   __shared__ float sQ[D][kRows + 4];
   __shared__ float sK[D][kKeys + 4];
   __shared__ double sRow[kRows];
   __shared__ int s_ok;
-  if (PROBS) {
+  if (MASKED) {
     if (threadIdx.x == 0) {
       const int32_t* hd = a.plan;
       s_ok = hd[H_MAGIC] == kPlanMagic && hd[H_VERSION] == kPlanVersion && hd[H_B] == a.B && hd[H_H] == a.H &&
@@ -79,7 +87,7 @@ __global__ void __launch_bounds__(kThreadsP) probs_kernel(ProbsArgs a) {
   stage_transposed<T, D>(sQ, q, a.qs, b, h, q0, a.S);
   const uint8_t* mrow = nullptr;
   int nq = 0;
-  if (PROBS && a.mask) {
+  if (MASKED && a.mask) {
     nq = a.S / a.bs;
     mrow = a.mask + (int64_t)((a.Bm == 1 ? 0 : b) * a.Hm + (a.Hm == 1 ? 0 : h)) * nq * nq;
   }
@@ -111,7 +119,7 @@ __global__ void __launch_bounds__(kThreadsP) probs_kernel(ProbsArgs a) {
         const int key = k0 + tj + j;
         float v = s[i][j] * a.scale;
         if (key >= a.S) v = -INFINITY;                      // outside the sequence: no weight
-        else if (PROBS) {
+        else if (MASKED) {
           bool keep = !a.causal || key <= row;
           if (keep && mrow) keep = mrow[(int64_t)(min(row, a.S - 1) / a.bs) * nq + key / a.bs] != 0;
           if (!keep) v = kMaskFill;
@@ -231,15 +239,15 @@ __global__ void __launch_bounds__(256) probs_heads_kernel(const double* __restri
   if (threadIdx.x == 0) head_sums[h] = red[0];
 }
 
-template <typename T, bool PROBS>
+template <typename T, int MODE>
 int launch(const ProbsArgs& a, int D, cudaStream_t s) {
   dim3 grid((a.S + kRows - 1) / kRows, a.B * a.H);
   switch (D) {
-    case 32: probs_kernel<T, 32, PROBS><<<grid, kThreadsP, 0, s>>>(a); break;
-    case 64: probs_kernel<T, 64, PROBS><<<grid, kThreadsP, 0, s>>>(a); break;
+    case 32: probs_kernel<T, 32, MODE><<<grid, kThreadsP, 0, s>>>(a); break;
+    case 64: probs_kernel<T, 64, MODE><<<grid, kThreadsP, 0, s>>>(a); break;
     default: return set_error(XSAKE_EUNSUPPORTED, "head_dim %d not in {32, 64}", D);
   }
-  return check_launch(PROBS ? "probs_kernel" : "entropy_qk_kernel");
+  return check_launch(MODE == kProbs ? "probs_kernel" : "entropy_qk_kernel");
 }
 
 }  // namespace
@@ -249,6 +257,66 @@ int plan_layout_from_dims(const XsakeMaskDims* d, PlanLayout* L);
 }  // namespace xsake
 
 using namespace xsake;
+
+namespace xsake {
+namespace {
+
+// Arguments of the masked modes from an attention descriptor and a compiled plan.
+int masked_args(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev, const void* k_dev, ProbsArgs* out) {
+  XSAKE_REQUIRE(desc && plan_dev && q_dev && k_dev, XSAKE_EINVAL, "NULL argument");
+  XSAKE_REQUIRE(desc->dtype == XSAKE_F32 || desc->dtype == XSAKE_BF16, XSAKE_EINVAL, "dtype %d", desc->dtype);
+  XSAKE_REQUIRE(desc->batch > 0 && desc->heads > 0 && desc->seq > 0, XSAKE_EINVAL, "dims must be positive");
+  XsakeMaskDims md{desc->batch, desc->heads, desc->seq, desc->mask_batch, desc->mask_heads, desc->block_size,
+                   desc->causal};
+  PlanLayout L;
+  int st = plan_layout_from_dims(&md, &L);
+  if (st) return st;
+  XSAKE_REQUIRE(((uintptr_t)plan_dev & 15) == 0, XSAKE_EINVAL, "plan must be 16-byte aligned");
+  XSAKE_REQUIRE((int64_t)desc->batch * desc->heads < 65536, XSAKE_EUNSUPPORTED, "too many (batch, head) slices");
+  ProbsArgs a{};
+  a.q = q_dev;
+  a.k = k_dev;
+  for (int i = 0; i < 3; ++i) {
+    a.qs[i] = desc->q_stride[i];
+    a.ks[i] = desc->k_stride[i];
+  }
+  a.B = desc->batch;
+  a.H = desc->heads;
+  a.S = desc->seq;
+  a.scale = desc->scale > 0.f ? desc->scale : 1.0f / sqrtf((float)desc->head_dim);
+  a.causal = desc->causal ? 1 : 0;
+  a.plan = reinterpret_cast<const int32_t*>(plan_dev);
+  a.mask = reinterpret_cast<const uint8_t*>(a.plan + L.mask_off);
+  a.Bm = L.Bm;
+  a.Hm = L.Hm;
+  a.bs = L.bs;
+  *out = a;
+  return XSAKE_OK;
+}
+
+}  // namespace
+}  // namespace xsake
+
+extern "C" int xsake_attn_entropy(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
+                                  const void* k_dev, double* head_sums_dev, void* workspace_dev,
+                                  size_t workspace_bytes, void* stream) {
+  clear_error();
+  ProbsArgs a;
+  int st = masked_args(desc, plan_dev, q_dev, k_dev, &a);
+  if (st) return st;
+  XSAKE_REQUIRE(head_sums_dev != nullptr, XSAKE_EINVAL, "NULL argument");
+  size_t need = 0;
+  xsake_entropy_qk_workspace_size(a.B, a.H, a.S, &need);
+  XSAKE_REQUIRE(workspace_dev && workspace_bytes >= need, XSAKE_EINVAL, "workspace too small: %zu < %zu bytes",
+                workspace_bytes, need);
+  a.partial = reinterpret_cast<double*>(workspace_dev);
+  cudaStream_t s = as_stream(stream);
+  int r = desc->dtype == XSAKE_F32 ? launch<float, kMaskedEntropy>(a, desc->head_dim, s)
+                                   : launch<__nv_bfloat16, kMaskedEntropy>(a, desc->head_dim, s);
+  if (r) return r;
+  probs_heads_kernel<<<(unsigned)a.H, 256, 0, s>>>(a.partial, a.B, a.H, (a.S + kRows - 1) / kRows, head_sums_dev);
+  return check_launch("probs_heads_kernel");
+}
 
 extern "C" int xsake_attn_probs(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
                                 const void* k_dev, float* p_dev, void* stream) {
@@ -283,8 +351,8 @@ extern "C" int xsake_attn_probs(const XsakeAttnDesc* desc, const void* plan_dev,
   a.bs = L.bs;
   a.p = p_dev;
   cudaStream_t s = as_stream(stream);
-  return desc->dtype == XSAKE_F32 ? launch<float, true>(a, desc->head_dim, s)
-                                  : launch<__nv_bfloat16, true>(a, desc->head_dim, s);
+  return desc->dtype == XSAKE_F32 ? launch<float, kProbs>(a, desc->head_dim, s)
+                                  : launch<__nv_bfloat16, kProbs>(a, desc->head_dim, s);
 }
 
 extern "C" int xsake_entropy_qk_workspace_size(int64_t batch, int64_t heads, int64_t seq, size_t* bytes) {
@@ -317,8 +385,8 @@ extern "C" int xsake_entropy_qk(int32_t dtype, const void* q_dev, const void* k_
   a.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim);
   a.partial = reinterpret_cast<double*>(workspace_dev);
   cudaStream_t s = as_stream(stream);
-  int r = dtype == XSAKE_F32 ? launch<float, false>(a, (int)head_dim, s)
-                             : launch<__nv_bfloat16, false>(a, (int)head_dim, s);
+  int r = dtype == XSAKE_F32 ? launch<float, kEntropy>(a, (int)head_dim, s)
+                             : launch<__nv_bfloat16, kEntropy>(a, (int)head_dim, s);
   if (r) return r;
   probs_heads_kernel<<<(unsigned)heads, 256, 0, s>>>(a.partial, a.B, a.H, (a.S + kRows - 1) / kRows,
                                                      head_sums_dev);

@@ -82,6 +82,32 @@ def entropy_head_sums_qk(q, k, scale: Optional[float] = None) -> torch.Tensor:
     return sums
 
 
+def entropy_head_sums_attention(q, k, block_mask, block_size: int, scale: Optional[float] = None,
+                                causal: bool = True) -> torch.Tensor:
+    """float64 [H] sums over (batch, query) of the row entropies of the attention weights that
+    ``sparse_attention(..., use_pallas=False)`` returns for this block mask (masked, causal cut,
+    finfo.min fill), computed on the GPU without materialising them.  These are the weights
+    the reference's calibration reduces (training/trainer.py:79-117 -> hads_pattern.py:36-50).
+    q, k: CUDA [B, H, S, D] tensors, any strides with a unit last stride."""
+    from .sparse_attention import _desc, _unit_last, compile_block_mask
+    dev.require_cuda()
+    q, k = (_unit_last(dev.to_device(t)[0]) for t in (q, k))
+    if q.dim() != 4 or k.shape != q.shape or k.dtype != q.dtype:
+        raise ValueError(f"q and k must be [batch, heads, seq, d_head] of one dtype, got {tuple(q.shape)} "
+                         f"{tuple(k.shape)}")
+    B, H, S, D = q.shape
+    cm = compile_block_mask(block_mask, B, H, S, block_size, causal, q.device)
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    _lib.check(lib.xsake_entropy_qk_workspace_size(B, H, S, C.byref(n)))
+    ws = dev.workspace(n.value, q.device)
+    sums = torch.empty(H, dtype=torch.float64, device=q.device)
+    d = _desc(q, k, k, q, cm, scale)
+    _lib.check(lib.xsake_attn_entropy(C.byref(d), cm.plan.data_ptr(), q.data_ptr(), k.data_ptr(), sums.data_ptr(),
+                                      ws.data_ptr(), ws.numel(), dev.stream_ptr()))
+    return sums
+
+
 def compute_attention_entropy_qk(q, k, scale: Optional[float] = None):
     """``compute_attention_entropy(softmax(q k^T * scale))`` (hads_pattern.py:36-50) fused: the
     calibration pass's entropies straight from q and k.  float32 [H] (NumPy for host input)."""

@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import math
 import weakref
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import List, Optional, Tuple
 
 import torch
@@ -30,8 +30,31 @@ from .fused_layernorm import fused_layernorm
 
 
 @dataclass
+class HADSConfig:
+    """model/config.py:8-15 (HADS calibration parameters)."""
+    min_sparsity: float = 0.10
+    max_sparsity: float = 0.90
+    calibration_steps: int = 10
+    block_size: int = 128
+    window_size: int = 2
+    entropy_temperature: float = 1.0
+
+
+@dataclass
+class KernelConfig:
+    """model/config.py:18-31 (attention kernel parameters)."""
+    block_size_q: int = 128
+    block_size_kv: int = 128
+    sparsity_type: str = "hads"
+    use_pallas: bool = True
+    hads: HADSConfig = field(default_factory=HADSConfig)
+
+
+@dataclass
 class ModelConfig:
-    """The fields of model/config.py the model reads (defaults: GPT-2 small, the reference's)."""
+    """The fields of model/config.py:34-58 the model reads (defaults: GPT-2 small, the
+    reference's).  The kernel parameters can be given either as the reference's nested
+    ``kernel=KernelConfig(...)`` or as the flat fields below; a ``kernel`` overrides them."""
     vocab_size: int = 50_257
     seq_len: int = 1_024
     n_layers: int = 12
@@ -40,11 +63,25 @@ class ModelConfig:
     d_ff: int = 3_072
     dropout: float = 0.0
     bias: bool = False
+    dtype: str = "bfloat16"
+    kernel: Optional[KernelConfig] = None
     block_size: int = 128
     sparsity_type: str = "hads"
     min_sparsity: float = 0.10
     max_sparsity: float = 0.90
     window_size: int = 2
+    calibration_steps: int = 10
+
+    def __post_init__(self):
+        k = self.kernel
+        if k is not None:
+            self.block_size, self.sparsity_type = k.block_size_q, k.sparsity_type
+            self.min_sparsity, self.max_sparsity = k.hads.min_sparsity, k.hads.max_sparsity
+            self.window_size, self.calibration_steps = k.hads.window_size, k.hads.calibration_steps
+
+    @property
+    def d_head(self) -> int:
+        return self.d_model // self.n_heads
 
 
 class LayerNorm(nn.Module):
@@ -84,11 +121,7 @@ class TransformerBlock(nn.Module):
     def __init__(self, cfg: ModelConfig, hads_profile: Optional[hp.HADSProfile] = None, device=None):
         super().__init__()
         self.ln1 = LayerNorm(cfg.d_model, device=device)
-        self.attn = XSAKEAttention(cfg.d_model, cfg.n_heads, cfg.n_layers, cfg.bias, cfg.dropout,
-                                   dtype=torch.float32, block_size=cfg.block_size,
-                                   sparsity_type=cfg.sparsity_type, hads_profile=hads_profile,
-                                   min_sparsity=cfg.min_sparsity, max_sparsity=cfg.max_sparsity,
-                                   window_size=cfg.window_size, device=device)
+        self.attn = XSAKEAttention(cfg, hads_profile, dtype=torch.float32, device=device)
         self.ln2 = LayerNorm(cfg.d_model, device=device)
         self.mlp = MLP(cfg, device=device)
 
@@ -114,9 +147,28 @@ class XSAKETransformer(nn.Module):
         self.ln_f = LayerNorm(cfg.d_model, device=device)
 
     def set_hads_profile(self, profile: hp.HADSProfile) -> None:
-        """Attach a (re)calibrated profile to every attention layer."""
+        """Attach a (re)calibrated profile to every attention layer (the reference rebuilds the
+        model with the new profile, training/trainer.py:191-200)."""
         for blk in self.blocks:
             blk.attn.hads_profile = profile
+
+    @torch.no_grad()
+    def layer0_qk(self, token_ids: torch.Tensor):
+        """The first attention layer's q and k for ``token_ids`` ([B, H, S, D] views of the
+        projections), with its block mask and block size: what calibration reduces (the
+        reference takes the first layer's weights, training/trainer.py:97-100).  Only the
+        embedding, the first LayerNorm and two projections run."""
+        S = token_ids.shape[1]
+        dtype = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled() else torch.float32
+        x = self.tok(token_ids).to(dtype) + self.pos[:S].to(dtype)
+        blk = self.blocks[0]
+        h = blk.ln1(x)
+        att = blk.attn
+        B = token_ids.shape[0]
+        q = att._heads(att.q_proj(h), B, S)
+        k = att._heads(att.k_proj(h), B, S)
+        mask, bs = att.get_block_mask(S)
+        return q, k, mask, bs, float(att.d_head ** -0.5)
 
     def forward(self, token_ids: torch.Tensor, collect_attn: bool = False
                 ) -> Tuple[torch.Tensor, Optional[List[torch.Tensor]]]:
