@@ -585,6 +585,7 @@ def run_secondary(args, dist, rank, world, masks, my_units, sets, cm):
     exch_ms = _reduce(t1.elapsed_time(t2), dist, "max")
     if comm is not None:
         comm.destroy()
+    del qk
     fl = 2 * 2 * Bc * Hc * Sc * Sc * Dc * NB
     out["calibration"] = {"value": fl / ((compute_ms + exch_ms) * 1e-3) / 1e12, "unit": "TFLOP/s",
                           "batches": NB, "compute_ms": compute_ms, "exchange_ms": exch_ms,
@@ -594,7 +595,43 @@ def run_secondary(args, dist, rank, world, masks, my_units, sets, cm):
                           "entropies": [round(float(e), 6) for e in ent],
                           "shape": "50 batches of fp32 Q, K [8, 12, 1024, 64], round-robin over ranks, fused "
                                    "QK -> entropy (xsake_entropy_qk)"}
+
+    # config-4 training step, data parallel (DDP gradient all-reduce over NCCL at N > 1)
+    out["train"] = train_step_timing(dist, rank, world, torch.cuda.current_device(), warmup=2, steps=4)
     return out
+
+
+def train_step_timing(dist, rank, world, local, warmup, steps):
+    """ms per step and whole-job tokens/s of the config-4 training step (12 layers, d=768, S=4096,
+    batch 8 per GPU, bf16 autocast over fp32 master weights, fused AdamW, DDP over the ranks)."""
+    import torch
+    from xsake_b200.model import ModelConfig, XSAKETransformer, cross_entropy_loss
+    cfg = ModelConfig(seq_len=4096, block_size=64)
+    torch.manual_seed(1234 + rank)
+    model = XSAKETransformer(cfg, device="cuda")
+    if dist is not None:
+        model = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], bucket_cap_mb=64)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, fused=True)
+    ids = [torch.randint(0, cfg.vocab_size, (8, cfg.seq_len), device="cuda") for _ in range(2)]
+
+    def step(i):
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, _ = model(ids[i % 2])
+            loss = cross_entropy_loss(logits, ids[i % 2])
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return loss
+
+    for i in range(warmup):
+        step(i)
+    ms = _time_calls(lambda it=iter(range(10 ** 9)): step(next(it)), steps, dist, warmup=0)
+    loss = float(step(0).detach().cpu())
+    del model, opt
+    torch.cuda.empty_cache()
+    return {"value": world * 8 * cfg.seq_len / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "parallelism": f"dp{world}" + (" (DDP, NCCL gradient all-reduce)" if world > 1 else ""),
+            "loss": loss, "shape": "12 layers d768 H12 S4096, batch 8 per GPU, bf16 autocast, AdamW"}
 
 
 def run_train(args, dist, rank, world, local):

@@ -84,6 +84,7 @@ using Clock = std::chrono::steady_clock;
 // deadline passes.  Returns XSAKE_OK, XSAKE_ECUDA (an NCCL error) or XSAKE_ETIMEOUT.
 int settle(Comm* cm, const char* what, Clock::time_point deadline) {
   const Nccl& n = nccl();
+  const auto spin_until = Clock::now() + std::chrono::microseconds(500);   // then back off
   for (;;) {
     ncclResult_t st = ncclInProgress;
     ncclResult_t r = n.get_async_error(cm->c, &st);
@@ -105,7 +106,10 @@ int settle(Comm* cm, const char* what, Clock::time_point deadline) {
       return set_error(XSAKE_ETIMEOUT, "%s: no progress within %d ms (a rank did not join); communicator aborted",
                        what, cm->timeout_ms);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    if (Clock::now() < spin_until)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(100));
   }
 }
 
@@ -191,6 +195,7 @@ extern "C" int xsake_comm_wait(void* comm, void* stream, int timeout_ms) {
   Comm* cm = static_cast<Comm*>(comm);
   XSAKE_REQUIRE(!cm->aborted, XSAKE_EINVAL, "communicator was aborted; destroy it");
   const auto deadline = deadline_of(timeout_ms);
+  const auto spin_until = Clock::now() + std::chrono::microseconds(500);
   for (;;) {
     const cudaError_t q = cudaStreamQuery(as_stream(stream));
     if (q == cudaSuccess) return XSAKE_OK;
@@ -207,7 +212,10 @@ extern "C" int xsake_comm_wait(void* comm, void* stream, int timeout_ms) {
       return set_error(XSAKE_ETIMEOUT, "xsake_comm_wait: the stream did not finish within %d ms; communicator "
                        "aborted", timeout_ms);
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(200));
+    if (Clock::now() < spin_until)
+      std::this_thread::yield();
+    else
+      std::this_thread::sleep_for(std::chrono::microseconds(100));
   }
 }
 
