@@ -13,8 +13,9 @@ NumPy-backed stand-in for ``jax`` / ``jax.numpy`` defined below.  What that pins
 What it cannot pin: XLA's exact float32 rounding/reduction order, and
 ``jnp.linspace`` (the stand-in restates JAX's formulation).
 
-Run from the repository root (needs the reference checkout):
-    python tests/golden/make_golden.py [/path/to/reference]
+Run from the repository root (needs the reference checkout), giving its location as the
+first argument or in XSAKE_REFERENCE:
+    python tests/golden/make_golden.py /path/to/reference
 """
 
 from __future__ import annotations
@@ -27,7 +28,9 @@ import types
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("XSAKE_REFERENCE", "")
+if __name__ == "__main__" and not (REF and os.path.isdir(REF)):
+    sys.exit("usage: make_golden.py /path/to/reference  (or set XSAKE_REFERENCE)")
 
 
 # ----------------------------------------------------------------------------- stand-in jax

@@ -17,39 +17,46 @@ import numpy as np
 SPARSITY_TYPES = ("dense", "local", "random", "bigbird")
 
 
+def _band(nb: int, half_width: int) -> np.ndarray:
+    """bool [nb, nb]: |i - j| <= half_width."""
+    idx = np.arange(nb)
+    return np.abs(idx[:, None] - idx[None, :]) <= half_width
+
+
 def make_block_mask(seq_len: int, block_size: int, sparsity_type: str, sparsity_ratio: float = 0.5,
                     window_size: int = 3, global_blocks: int = 1, causal: bool = False,
                     rng: Optional[int] = None) -> np.ndarray:
-    """bool [nb, nb] block mask of ``sparsity_type`` (sparsity_mask.py:25-102)."""
+    """bool [nb, nb] block mask of ``sparsity_type`` (sparsity_mask.py:25-102).
+
+    The seeded patterns draw with NumPy's ``Generator.choice`` row by row, in the reference's
+    order and over the same candidate sets, so the masks are the reference's bit for bit."""
     if seq_len % block_size != 0:
-        raise ValueError("seq_len must be divisible by block_size")
+        raise ValueError(f"block_size {block_size} does not divide seq_len {seq_len}")
     nb = seq_len // block_size
     if sparsity_type == "dense":
         mask = np.ones((nb, nb), dtype=bool)
     elif sparsity_type == "local":
-        mask = np.zeros((nb, nb), dtype=bool)
-        for i in range(nb):
-            mask[i, max(0, i - window_size):min(nb, i + window_size + 1)] = True
+        mask = _band(nb, window_size)
     elif sparsity_type == "random":
-        keep = max(1, int(nb * (1.0 - sparsity_ratio)))
-        mask = np.zeros((nb, nb), dtype=bool)
+        per_row = max(1, int(nb * (1.0 - sparsity_ratio)))
         gen = np.random.default_rng(0 if rng is None else int(rng))
-        for i in range(nb):
-            mask[i, gen.choice(nb, size=keep, replace=False)] = True
-    elif sparsity_type == "bigbird":
         mask = np.zeros((nb, nb), dtype=bool)
-        g = min(global_blocks, nb)
-        rand_keep = max(1, int(nb * 0.15))
+        for row in mask:
+            row[gen.choice(nb, size=per_row, replace=False)] = True
+    elif sparsity_type == "bigbird":
+        # Fixed part first (leading columns + band around the diagonal), then per row a seeded
+        # draw of up to 15% of the blocks among the columns the fixed part leaves out.
+        mask = _band(nb, window_size)
+        mask[:, :min(global_blocks, nb)] = True
+        extra = max(1, int(nb * 0.15))
         gen = np.random.default_rng(42)
-        for i in range(nb):
-            mask[i, :g] = True                                            # global blocks
-            mask[i, max(0, i - window_size):min(nb, i + window_size + 1)] = True   # local window
-            candidates = np.where(~mask[i])[0]                            # random long range
-            if len(candidates) > 0:
-                mask[i, gen.choice(candidates, size=min(rand_keep, len(candidates)), replace=False)] = True
+        for row in mask:
+            free = np.flatnonzero(~row)
+            if free.size:
+                row[gen.choice(free, size=min(extra, free.size), replace=False)] = True
     else:
-        raise ValueError(f"Unknown sparsity_type '{sparsity_type}'. For 'hads', use "
-                         "xsake_b200.hads_pattern.build_hads_profile().")
+        raise ValueError(f"sparsity_type must be one of {SPARSITY_TYPES} (got {sparsity_type!r}); "
+                         "HADS masks come from xsake_b200.hads_pattern.build_hads_profile()")
     if causal:
         mask &= np.tri(nb, nb, dtype=bool)
     return mask
