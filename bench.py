@@ -515,7 +515,13 @@ def run_secondary(args, dist, rank, world, masks, my_units, sets, cm):
                                                            bt.data_ptr(), 1e-5, ys[i].data_ptr(), None, None, sp())
                        for i in range(12)], dist)
     gbs = (8192 * 768 * 4 + 2 * 768 * 4) / (ms * 1e-3) / 1e9
+    # the same bytes moved by a plain device copy in the same graph setup: what this size allows
+    def copy_call(i):
+        ys[i].copy_(xs[i])
+        return 0
+    cms = _graph_calls([lambda i=i: copy_call(i) for i in range(12)], dist)
     out["layernorm"] = {"value": gbs, "unit": "GB/s", "ms_per_call": ms, "frac_of_hbm_per_gpu": gbs / world / hbm,
+                        "copy_ms_per_call": cms, "frac_of_copy_same_bytes": cms / ms,
                         "shape": "bf16 [8192, 768], fp32 gamma/beta, rows split over ranks"}
     del xs, ys
 
