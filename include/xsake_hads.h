@@ -80,11 +80,18 @@ XSAKE_API int xsake_mask_compile(const XsakeMaskDims* dims, const uint8_t* mask_
  * number of tile workers the forward runs concurrently (0 = 2 x the SM count of the current
  * device); the plan splits a query tile's kv walk into pieces when it is long next to the
  * average load of a worker, so a small job still fills the GPU.  Invalid unit ids are left out
- * and recorded in the device error word. */
+ * and recorded in the device error word.  forward_pairing (one of XSAKE_PAIRING_*) fixes how the
+ * tensor-core forward groups rows into work items; AUTO lets the plan compiler choose from the
+ * mask, the others exist for measurement and tests (every pairing gives the same results up to
+ * fp32 rounding of the softmax statistics). */
+#define XSAKE_PAIRING_AUTO 0
+#define XSAKE_PAIRING_QUERY 1   /* query chunks 2t, 2t+1 of one unit            */
+#define XSAKE_PAIRING_UNITS 2   /* query chunk j of two units that share the mask */
 typedef struct {
   const int32_t* units_dev;
   int32_t n_units;
   int32_t workers;
+  int32_t forward_pairing;
 } XsakePlanOptions;
 
 XSAKE_API int xsake_mask_compile_ex(const XsakeMaskDims* dims, const XsakePlanOptions* options,
@@ -103,7 +110,7 @@ typedef struct {
   int64_t empty_qblocks;    /* fully masked q-blocks                                       */
   int32_t work_items;       /* forward work items, split pieces included                   */
   int32_t selected_units;   /* (b, h) units the plan computes                              */
-  int32_t unit_pairing;     /* 1: the forward pairs two units per item, 0: two query chunks */
+  int32_t pairing;          /* forward pairing: 0 query chunks, 1 units                    */
   int32_t split_items;      /* work items cut into pieces over their kv chunks             */
   int32_t split_slots;      /* partial slots those pieces use                              */
   int32_t split_cap;        /* largest piece, in 64-key chunks                             */

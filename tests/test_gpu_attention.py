@@ -159,6 +159,51 @@ def test_forward_pairing_follows_the_mask():
         assert st["computed_tiles"] >= st["active_blocks"]
 
 
+def _pairing_masks():
+    """Masks for the forced-pairing tests: HADS causal and not, odd chunk counts with empty
+    rows, a dense causal mask, block 128 and a mask per unit."""
+    odd = oh.dummy_hads_profile(2, 320, 64, causal=True).block_masks.copy()
+    odd[1, 2, :] = False
+    odd[0, 4, :4] = False
+    per_unit = np.stack([oh.dummy_hads_profile(3, 512, 64, causal=True, global_blocks=b).block_masks
+                         for b in range(2)])
+    return [
+        (2, 4, 512, 64, True, oh.dummy_hads_profile(4, 512, 64, causal=True, global_blocks=1).block_masks),
+        (2, 4, 512, 64, False, oh.dummy_hads_profile(4, 512, 64, causal=False, global_blocks=0).block_masks),
+        (3, 2, 320, 64, True, odd),
+        (3, 2, 320, 64, False, odd),
+        (2, 2, 512, 64, True, np.ones((8, 8), bool)),
+        (1, 3, 1024, 128, True, oh.dummy_hads_profile(3, 1024, 128, causal=True).block_masks),
+        (2, 3, 512, 64, True, per_unit),
+    ]
+
+
+@pytest.mark.parametrize("case", range(7))
+def test_every_forward_pairing_matches_oracle(case):
+    # The plan option forces each of the tensor-core forward's role sets (query-chunk pairs, unit
+    # pairs) on the same inputs, whatever the mask would choose: each matches the oracle, and
+    # they agree with one another to bf16 output rounding.
+    sa = _sa()
+    B, H, S, bs, causal, mask = _pairing_masks()[case]
+    q, k, v = (_bf16_round(_rand((B, H, S, 64), 700 + 10 * case + i)) for i in range(3))
+    tq, tk, tv = (torch.from_numpy(x).to(torch.bfloat16).cuda() for x in (q, k, v))
+    ref, _, lse_ref = oa.sparse_attention_reference(q, k, v, mask, bs, causal=causal, return_weights=False,
+                                                    return_lse=True)
+    live = lse_ref > -1e30
+    outs = {}
+    for pairing in ("query_chunk", "unit"):
+        cm = sa.compile_block_mask(mask, B, H, S, bs, causal, pairing=pairing)
+        assert cm.stats()["pairing"] == pairing
+        out, lse = sa.attention_forward(tq, tk, tv, cm, bs, None, causal)
+        o = out.float().cpu().numpy()
+        assert np.isfinite(o).all(), pairing
+        assert _err(o, ref) <= BF16_TOL * np.abs(ref).max(), (pairing, _err(o, ref))
+        np.testing.assert_allclose(lse.cpu().numpy()[live], lse_ref[live], rtol=0, atol=2e-2)
+        outs[pairing] = o
+    for pairing, o in outs.items():
+        assert _err(o, outs["query_chunk"]) <= 1e-2 * np.abs(ref).max(), pairing
+
+
 def test_bf16_bshd_layout_and_scale():
     prof = oh.dummy_hads_profile(4, 256, 64, causal=True)
     _bf16_case(2, 4, 256, 64, 64, True, prof.block_masks, seed=40, layout="bshd", scale=0.2)

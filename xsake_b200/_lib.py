@@ -31,12 +31,13 @@ class MaskDims(C.Structure):
 
 
 class PlanOptions(C.Structure):
-    _fields_ = [("units_dev", C.c_void_p), ("n_units", C.c_int32), ("workers", C.c_int32)]
+    _fields_ = [("units_dev", C.c_void_p), ("n_units", C.c_int32), ("workers", C.c_int32),
+                ("forward_pairing", C.c_int32)]
 
 
 class PlanInfo(C.Structure):
     _fields_ = [("active_blocks", C.c_int64), ("computed_tiles", C.c_int64), ("empty_qblocks", C.c_int64),
-                ("work_items", C.c_int32), ("selected_units", C.c_int32), ("unit_pairing", C.c_int32),
+                ("work_items", C.c_int32), ("selected_units", C.c_int32), ("pairing", C.c_int32),
                 ("split_items", C.c_int32), ("split_slots", C.c_int32), ("split_cap", C.c_int32),
                 ("workers", C.c_int32), ("reserved", C.c_int32)]
 

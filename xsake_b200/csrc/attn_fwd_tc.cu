@@ -272,6 +272,58 @@ struct FwdCtx {
   const int32_t* entries;
 };
 
+// Row max of 64 raw scores: a depth-4 tree of 3-input maxes.
+__device__ __forceinline__ float rowmax64(const float* x) {
+  float t1[22];
+#pragma unroll
+  for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+  t1[21] = x[63];
+  float t2[8];
+#pragma unroll
+  for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
+  t2[7] = t1[21];
+  return fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
+}
+
+// Output rows of a query-chunk-pairing item (tile_roles) once the row's O (64 fp32),
+// running max m (log2 units) and sum l are in registers: the split merge (a piece that leaves it
+// to another piece writes nothing), O / l in bf16, the uniform attention of rows with no live
+// score, and lse.  The whole warp calls it.
+__device__ __forceinline__ void tile_output(const TcParams& p, const FwdCtx& c, int X, int row, int32_t wk, float m,
+                                            float l, float (&o)[64], uint32_t& ep_phase, bool& ok) {
+  const AttnArgs& a = p.a;
+  const int grp = work_word(wk, 6), parts = work_word(wk, 5);
+  if (grp >= 0 && !split_finish(p, grp, parts >> 8, parts & 0xff, work_word(wk, 7), row, &c.bars->ep_bar[X],
+                                ep_phase, c.ep_flag + X, m, l, o, c.abort, ok))
+    return;   // another piece of this item merges the rows (or a wait failed: ok is false)
+  const int u0 = work_word(wk, 0);
+  const Item we{u0 / a.H, u0 % a.H, work_word(wk, 2), 0, 0};
+  const int tok = 128 * we.u + row;
+  const bool valid = tok < a.S;
+  const bool empty = valid && !(l > 0.f);
+  uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + we.b * a.os[0] +
+                                           we.h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
+  if (valid && !empty) store_o_row(orow_g, o, 1.f / l);
+  if (__any_sync(0xffffffffu, empty)) {
+    // Rows with no live score: the reference's finfo.min fill makes them attend uniformly.
+    float2 mine;
+    warp_mean_v(a, we.b, we.h, mine);
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      uint32_t wv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int src = 4 * cc + q;   // column pair index 0..31
+        __nv_bfloat162 pb = __floats2bfloat162_rn(__shfl_sync(0xffffffffu, mine.x, src),
+                                                  __shfl_sync(0xffffffffu, mine.y, src));
+        wv[q] = *reinterpret_cast<uint32_t*>(&pb);
+      }
+      if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+  }
+  if (valid) a.lse[(int64_t)(we.b * a.H + we.h) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
+}
+
 // Roles of the query-chunk pairing: a work item is query chunks 2t, 2t+1 of one (b, h).
 __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtensorMap& tmK,
                                            const CUtensorMap& tmV, const TcParams& p, const FwdCtx& c) {
@@ -530,18 +582,7 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
               for (int j = 0; j < 64; ++j)
                 if (j > diag_lim) x[j] = -INFINITY;
             }
-            // Row max of the raw scores: a depth-4 tree of 3-input maxes.
-            float t1[22];
-#pragma unroll
-            for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
-            t1[21] = x[63];
-            float t2[8];
-#pragma unroll
-            for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
-            t2[7] = t1[21];
-            const float mraw =
-                fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
-            const float mx = mraw * p.scale_log2;       // log2 units (scale > 0)
+            const float mx = rowmax64(x) * p.scale_log2;   // log2 units (scale > 0)
             const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
             if (m == -INFINITY) m = mx;
             // TMEM loads/stores are warp-collective: the whole warp rescales when any row must.
@@ -622,38 +663,7 @@ __device__ __forceinline__ void tile_roles(const CUtensorMap& tmQ, const CUtenso
 #pragma unroll
         for (int j = 0; j < 64; ++j) o[j] = 0.f;
       }
-      const int grp = work_word(wk, 6), parts = work_word(wk, 5);
-      if (grp >= 0 && !split_finish(p, grp, parts >> 8, parts & 0xff, work_word(wk, 7), row, &bars->ep_bar[X],
-                                    ep_phase, c.ep_flag + X, m, l, o, abort, ok)) {
-        if (!ok) break;
-        continue;   // another piece of this item merges the rows
-      }
-      const int u0 = work_word(wk, 0);
-      const Item we{u0 / a.H, u0 % a.H, work_word(wk, 2), 0, 0};
-      const int tok = 128 * we.u + row;
-      const bool valid = tok < a.S;
-      const bool empty = valid && !(l > 0.f);
-      uint4* orow_g = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.o) + we.b * a.os[0] +
-                                               we.h * a.os[1] + (int64_t)(valid ? tok : 0) * a.os[2]);
-      if (valid && !empty) store_o_row(orow_g, o, 1.f / l);
-      if (__any_sync(0xffffffffu, empty)) {
-        // Rows with no live score: the reference's finfo.min fill makes them attend uniformly.
-        float2 mine;
-        warp_mean_v(a, we.b, we.h, mine);
-#pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
-          uint32_t wv[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int src = 4 * cc + q;   // column pair index 0..31
-            __nv_bfloat162 pb = __floats2bfloat162_rn(__shfl_sync(0xffffffffu, mine.x, src),
-                                                      __shfl_sync(0xffffffffu, mine.y, src));
-            wv[q] = *reinterpret_cast<uint32_t*>(&pb);
-          }
-          if (empty) orow_g[cc] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-        }
-      }
-      if (valid) a.lse[(int64_t)(we.b * a.H + we.h) * a.S + tok] = empty ? kMaskFill : (m + __log2f(l)) * kLn2;
+      tile_output(p, c, X, row, wk, m, l, o, ep_phase, ok);
     }
     if (!ok) fail(abort, 4);
   }
@@ -988,17 +998,7 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
             for (int j = 0; j < 64; ++j)
               if (j > lim) x[j] = -INFINITY;
           }
-          float t1[22];
-#pragma unroll
-          for (int j = 0; j < 21; ++j) t1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
-          t1[21] = x[63];
-          float t2[8];
-#pragma unroll
-          for (int j = 0; j < 7; ++j) t2[j] = max3(t1[3 * j], t1[3 * j + 1], t1[3 * j + 2]);
-          t2[7] = t1[21];
-          const float mraw =
-              fmaxf(max3(t2[0], t2[1], t2[2]), max3(t2[3], t2[4], fmaxf(t2[5], fmaxf(t2[6], t2[7]))));
-          const float mx = mraw * p.scale_log2;
+          const float mx = rowmax64(x) * p.scale_log2;
           const bool need = (m != -INFINITY) && (mx > m + kRescaleThreshold);
           if (m == -INFINITY) m = mx;
           if (__any_sync(0xffffffffu, need)) {
@@ -1167,7 +1167,7 @@ tc_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ C
   if (*plan_ok) {
     const FwdCtx c{smem, bars, abort, item_slots, ep_flag, tmem, a.plan + L.f_entries_off};
     // The plan compiler chose the pairing from the mask (H_FWD_PAIR); every CTA reads the same word.
-    if (a.plan[H_FWD_PAIR])
+    if (a.plan[H_FWD_PAIR] == kPairUnits)
       pair_roles(tmQ, tmK, tmV, p, c);
     else
       tile_roles(tmQ, tmK, tmV, p, c);

@@ -248,7 +248,7 @@ __device__ void warp_sort_desc(int n, int maxc, C cost_of, int32_t* out, int32_t
 }
 
 __global__ void __launch_bounds__(kWorkThreads) plan_work_kernel(PlanLayout L, int32_t* __restrict__ plan,
-                                                                 int32_t workers) {
+                                                                 int32_t workers, int32_t pairing) {
   extern __shared__ int32_t smem[];   // 2 * (n64 + 2) histogram words
   __shared__ long long s_red[32];
   __shared__ int3 s_red3[32];
@@ -339,15 +339,17 @@ __global__ void __launch_bounds__(kWorkThreads) plan_work_kernel(PlanLayout L, i
     useful = block_sum(use, s_red);
     bool pairs_possible = false;
     for (int g = 0; g < L.ngroups && !pairs_possible; ++g) pairs_possible = grp_off[g + 1] - grp_off[g] >= 2;
-    fwd_pair = (pairs_possible && 100 * useful < 88 * (2 * entries)) ? 1 : 0;
-    tiles = fwd_pair ? useful : 2 * entries;
+    const int32_t auto_pair = (pairs_possible && 100 * useful < 88 * (2 * entries)) ? kPairUnits : kPairQuery;
+    fwd_pair = pairing == XSAKE_PAIRING_QUERY ? kPairQuery : pairing == XSAKE_PAIRING_UNITS ? kPairUnits : auto_pair;
+    const bool units = fwd_pair == kPairUnits;
+    tiles = units ? useful : 2 * entries;
 
     // 5. Base work items and their steps (kv chunks walked).
     const int PT = grp_poff[L.ngroups];
-    const int n_base = fwd_pair ? L.n64 * PT : nsel_items;
+    const int n_base = units ? L.n64 * PT : nsel_items;
     int32_t* base_cost = plan + L.f_order_off;   // reused by the final sort below
     auto describe = [&](int i, FWork& w, int& row) {
-      if (fwd_pair) {
+      if (units) {
         const int jj = i / PT, rem = i % PT;
         const int j = L.n64 - 1 - jj;
         int lo = 0, hi = L.ngroups - 1;   // group g with grp_poff[g] <= rem < grp_poff[g + 1]
@@ -427,7 +429,7 @@ __global__ void __launch_bounds__(kWorkThreads) plan_work_kernel(PlanLayout L, i
             if (n == 1) {
               x.lo = 0;
               x.hi = rowcnt;
-            } else if (!fwd_pair) {   // every entry of a pair row is a step of its tile
+            } else if (!units) {      // every entry of a pair row is a step of its tile
               x.lo = s0;
               x.hi = s1;
             } else {                  // steps are the entries half j % 2 attends
@@ -465,7 +467,7 @@ __global__ void __launch_bounds__(kWorkThreads) plan_work_kernel(PlanLayout L, i
     // longest first by steps (stable).
     __syncthreads();
     int32_t* order = plan + L.f_order_off;
-    if (fwd_pair) {
+    if (units) {
       for (int i = tid; i < n_work; i += blockDim.x) order[i] = i;
     } else if (warp == 0) {
       warp_sort_desc(n_work, L.n64, [&](int i) { return piece_cost[i]; }, order, smem);
@@ -543,11 +545,14 @@ extern "C" int xsake_mask_compile_ex(const XsakeMaskDims* dims, const XsakePlanO
                 "plan buffer too small: %zu < %lld bytes", plan_bytes, (long long)L.total_words * 4);
   XSAKE_REQUIRE(((uintptr_t)plan_dev & 15) == 0, XSAKE_EINVAL, "plan must be 16-byte aligned");
   const int32_t* units = nullptr;
-  int32_t n_units = 0, workers = 0;
+  int32_t n_units = 0, workers = 0, pairing = XSAKE_PAIRING_AUTO;
   if (opt) {
     units = opt->units_dev;
     n_units = opt->n_units;
     workers = opt->workers;
+    pairing = opt->forward_pairing;
+    XSAKE_REQUIRE(pairing >= XSAKE_PAIRING_AUTO && pairing <= XSAKE_PAIRING_UNITS, XSAKE_EINVAL,
+                  "forward_pairing %d is not one of XSAKE_PAIRING_*", pairing);
     XSAKE_REQUIRE(units != nullptr || n_units == 0, XSAKE_EINVAL, "n_units %d without a unit list", n_units);
     XSAKE_REQUIRE(units == nullptr || (n_units > 0 && n_units <= dims->batch * dims->heads), XSAKE_EINVAL,
                   "n_units %d must be in [1, batch * heads = %d]", n_units, dims->batch * dims->heads);
@@ -570,7 +575,7 @@ extern "C" int xsake_mask_compile_ex(const XsakeMaskDims* dims, const XsakePlanO
   }
   const size_t smem = 2 * (size_t)(L.n64 + 2) * sizeof(int32_t);
   XSAKE_REQUIRE(smem <= 48 * 1024, XSAKE_EUNSUPPORTED, "seq too long for the plan compiler");
-  plan_work_kernel<<<1, kWorkThreads, smem, s>>>(L, (int32_t*)plan_dev, workers);
+  plan_work_kernel<<<1, kWorkThreads, smem, s>>>(L, (int32_t*)plan_dev, workers, pairing);
   return check_launch("plan_work_kernel");
 }
 
@@ -593,7 +598,7 @@ extern "C" int xsake_mask_plan_info(const void* plan_dev, void* stream, XsakePla
   info->empty_qblocks = u64(H_EMPTY_LO);
   info->work_items = hdr[H_F_WORK];
   info->selected_units = hdr[H_SEL_UNITS];
-  info->unit_pairing = hdr[H_FWD_PAIR];
+  info->pairing = hdr[H_FWD_PAIR];
   info->split_items = hdr[H_SPLIT_GROUPS];
   info->split_slots = hdr[H_SPLIT_SLOTS];
   info->split_cap = hdr[H_SPLIT_CAP];

@@ -53,6 +53,11 @@ constexpr int kSplitSlots = 512;            // partial slots in the forward work
 constexpr int kMaxPieces = 64;              // pieces of one item at most
 constexpr int kMinPieceSteps = 4;           // smallest piece (kv chunks)
 
+// Forward pairings (header word H_FWD_PAIR): which rows a work item of the tensor-core forward
+// covers; every step is one 64-key chunk.
+constexpr int32_t kPairQuery = 0;   // query chunks 2t, 2t+1 of one unit
+constexpr int32_t kPairUnits = 1;   // query chunk j of two units that share the mask
+
 // Forward work table entry (8 int32 words).
 struct FWork {
   int32_t u0;      // unit b * H + h (query-chunk pairing: the unit; unit pairing: unit of lanes 0-15)
@@ -74,7 +79,7 @@ enum PlanHeader : int {
   H_F_WORK,         // f_work entries
   H_ACTIVE_LO, H_ACTIVE_HI, H_TILES_LO, H_TILES_HI, H_EMPTY_LO, H_EMPTY_HI,
   H_ITEMS_LO, H_ITEMS_HI,
-  H_FWD_PAIR,       // 1: the forward pairs units that share a mask (see attn_fwd_tc.cu), 0: query chunks
+  H_FWD_PAIR,       // forward pairing (kPairQuery or kPairUnits; see attn_fwd_tc.cu)
   H_SPLIT_GROUPS,   // split work items
   H_SPLIT_SLOTS,    // partial slots they use
   H_SPLIT_CAP,      // largest piece (kv chunks) the split rule allowed

@@ -77,7 +77,7 @@ class CompiledMask:
             self._stats = {"active_blocks": info.active_blocks, "computed_tiles": info.computed_tiles,
                            "empty_qblocks": info.empty_qblocks, "work_items": info.work_items,
                            "selected_units": info.selected_units,
-                           "pairing": "unit" if info.unit_pairing else "query_chunk",
+                           "pairing": _PAIRING_NAMES.get(info.pairing, str(info.pairing)),
                            "split_items": info.split_items, "split_slots": info.split_slots,
                            "split_cap": info.split_cap, "workers": info.workers}
         return self._stats
@@ -137,13 +137,22 @@ _CACHE: "OrderedDict[tuple, CompiledMask]" = OrderedDict()
 _CACHE_MAX = 32
 
 
+_PAIRINGS = {"auto": 0, "query_chunk": 1, "unit": 2}
+_PAIRING_NAMES = {0: "query_chunk", 1: "unit"}
+
+
 def compile_block_mask(block_mask, batch: int, heads: int, seq: int, block_size: int,
-                       causal: bool, device=None, units=None, workers: int = 0) -> CompiledMask:
+                       causal: bool, device=None, units=None, workers: int = 0,
+                       pairing: str = "auto") -> CompiledMask:
     """Compile ``block_mask`` (broadcast like ``_broadcast_mask``) into a device plan.
 
     ``units`` (unit ids ``b * heads + h``; None = all) restricts the plan to those (batch,
     head) units.  ``workers`` (0 = two per SM of the device) is the concurrency the forward's
-    split rule assumes."""
+    split rule assumes.  ``pairing`` fixes how the tensor-core forward groups rows into work
+    items ("query_chunk": chunks 2t, 2t+1 of one unit; "unit": chunk j of two units that share
+    the mask); "auto" lets the plan compiler choose from the mask."""
+    if pairing not in _PAIRINGS:
+        raise ValueError(f"pairing must be one of {sorted(_PAIRINGS)}, got {pairing!r}")
     dev.require_cuda()
     units = _units_tuple(units, batch, heads)
     if isinstance(block_mask, CompiledMask):
@@ -168,7 +177,7 @@ def compile_block_mask(block_mask, batch: int, heads: int, seq: int, block_size:
         raise ValueError(f"block_mask leading dims {(Bm, Hm)} do not broadcast to {(batch, heads)}")
     device = device or torch.device("cuda", torch.cuda.current_device())
     key = (_mask_key(m, id(block_mask)), batch, heads, seq, block_size, bool(causal), str(device), units,
-           int(workers))
+           int(workers), pairing)
     hit = _CACHE.get(key)
     if hit is not None:
         _CACHE.move_to_end(key)
@@ -185,7 +194,7 @@ def compile_block_mask(block_mask, batch: int, heads: int, seq: int, block_size:
     if units is not None:
         ut = torch.tensor(units, dtype=torch.int32).to(device)
     opts = _lib.PlanOptions(ut.data_ptr() if ut is not None else None, len(units) if units else 0,
-                            int(workers))
+                            int(workers), _PAIRINGS[pairing])
     _lib.check(lib.xsake_mask_compile_ex(C.byref(dims), C.byref(opts), mt.data_ptr(), plan.data_ptr(),
                                          nbytes.value, dev.stream_ptr()))
     cm = CompiledMask(plan, dims, units)
