@@ -810,11 +810,12 @@ def run_rowop(args, dist, rank, world, local):
             "note": "secondary row; not the headline"}
     line.update(extra)
     if wl == "calib":
-        fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
-        line["roofline"] = {"bound": "fp32 CUDA cores", "achieved": value, "peak": fp32_peak, "unit": "TFLOP/s",
-                            "frac": value / fp32_peak,
-                            "peak_source": "nominal fp32 FMA rate (148 SMs x 128 lanes x 2 x 1.965 GHz); "
-                                           "not in the measured peaks"}
+        # The tensor cores run six bf16 products per fp32 product (three bf16 parts an operand).
+        peak_tf, _, kind_tf = _peaks()
+        mma_tf = 6 * value
+        line["roofline"] = {"bound": "tensor", "achieved": mma_tf, "peak": peak_tf, "unit": "TFLOP/s",
+                            "frac": mma_tf / peak_tf, "peak_source": f"bf16_tflops ({kind_tf})",
+                            "work": "bf16 MMA FLOPs = 6 x the fp32 QK^T FLOPs of the two passes"}
     elif unit == "GB/s":
         line["roofline"] = {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s", "frac": value / hbm,
                             "peak_source": f"hbm_gbs ({kind})"}

@@ -229,7 +229,10 @@ XSAKE_API int xsake_entropy_rows(const float* p_dev, int64_t batch, int64_t head
  * [B, H, S, D] (fp32 or bf16, D 32 or 64), no mask (the calibration pass attends fully,
  * hads_pattern.py:118-166 via training/trainer.py:79-117); scale <= 0 selects 1/sqrt(D).
  * head_sums_dev[h] = sum over (b, q) of the clipped row entropy, as xsake_entropy_rows gives for
- * the materialised P.  fp32 scores on the CUDA cores; deterministic. */
+ * the materialised P.  D = 64: tensor cores, an fp32 operand split into three bf16 parts whose
+ * six leading products give fp32-accurate scores (bf16 inputs: one product); D = 32: fp32 on
+ * the CUDA cores.  Deterministic.  The workspace (xsake_entropy_qk_workspace_size bytes, 256-byte
+ * aligned) holds the per-tile partial sums and the bf16 parts of K (~3 * B * H * S * 128 bytes). */
 XSAKE_API int xsake_entropy_qk_workspace_size(int64_t batch, int64_t heads, int64_t seq, size_t* bytes);
 XSAKE_API int xsake_entropy_qk(int32_t dtype, const void* q_dev, const void* k_dev, int64_t batch,
                        int64_t heads, int64_t seq, int64_t head_dim, float scale,

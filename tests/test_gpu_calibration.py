@@ -92,6 +92,24 @@ def test_entropy_qk_matches_oracle(S):
     assert np.max(np.abs(got - ref) / np.abs(ref)) <= ENT_RTOL, np.max(np.abs(got - ref) / np.abs(ref))
 
 
+@pytest.mark.parametrize("dtype,D,S", [("bf16", 64, 320), ("f32", 32, 320), ("f32", 64, 129)])
+def test_entropy_qk_dtypes_head_dims_and_tails(dtype, D, S):
+    # bf16 inputs take one product on the tensor cores (bf16 products are exact); head_dim 32
+    # stays on the CUDA cores; S = 129 leaves one live row in the second 128-row tile and one
+    # live key in the last 64-key chunk.
+    from xsake_b200 import hads_pattern as hp
+    q, k = _rand((2, 3, S, D), 560), _rand((2, 3, S, D), 561)
+    q *= np.linspace(0.5, 3.0, 3, dtype=np.float32)[None, :, None, None]
+    tq, tk = torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda()
+    if dtype == "bf16":
+        q, k = (oi.to_bf16(x).astype(np.float32) for x in (q, k))
+        tq, tk = tq.to(torch.bfloat16), tk.to(torch.bfloat16)
+    scale = D ** -0.5
+    got = hp.compute_attention_entropy_qk(tq, tk, scale).cpu().numpy()
+    ref = oh.compute_attention_entropy(_softmax64(q, k, scale))
+    assert np.max(np.abs(got - ref) / np.abs(ref)) <= ENT_RTOL, np.max(np.abs(got - ref) / np.abs(ref))
+
+
 def test_entropy_qk_matches_materialised_path_on_calibration_batch():
     """Config 2's calibration batch shape (B=8, H=12, S=1024, D=64, fp32, q scaled by tau):
     fused entropies == drop-in path (weights, then xsake_entropy_rows) == oracle on 2 batches."""
@@ -138,6 +156,23 @@ def test_masked_entropy_matches_weights_entropy(dtype, layout):
     _, ref_p = oa.sparse_attention_reference(q, k, k, m, bs, causal=True)
     ref = oh.entropy_head_sums(ref_p)
     assert np.max(np.abs(sums - ref) / np.abs(ref)) <= ENT_RTOL
+
+
+@pytest.mark.parametrize("bs,causal,S", [(32, True, 320), (128, False, 384), (64, False, 192)])
+def test_masked_entropy_block_sizes(bs, causal, S):
+    # Block sizes below, at and above the 64-key chunk of the tensor-core kernel, with and
+    # without the causal cut; one fully masked q-block.
+    from xsake_b200 import hads_pattern as hp
+    B, H, D = 2, 2, 64
+    m = oh.dummy_hads_profile(H, S, bs, causal=causal, global_blocks=1).block_masks.copy()
+    m[1, 1, :] = False
+    q, k = _rand((B, H, S, D), 610 + bs), _rand((B, H, S, D), 611 + bs)
+    q *= np.float32(2.0)
+    sums = hp.entropy_head_sums_attention(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(), m, bs, None,
+                                          causal=causal).cpu().numpy()
+    _, ref_p = oa.sparse_attention_reference(q, k, k, m, bs, causal=causal)
+    ref = oh.entropy_head_sums(ref_p)
+    assert np.max(np.abs(sums - ref) / np.abs(ref)) <= ENT_RTOL, np.max(np.abs(sums - ref) / np.abs(ref))
 
 
 def test_model_calibration_and_recalibration_step():

@@ -46,6 +46,14 @@ bool tc_attn_fwd_supported(const AttnArgs& a, int dtype);
 int tc_attn_bwd(const AttnArgs& a, void* ws, size_t ws_bytes, cudaStream_t s);
 bool tc_attn_bwd_supported(const AttnArgs& a, int dtype);
 
+// Block mask of the entropy of masked weights (xsake_attn_entropy): the compiled plan (header
+// checked on the device) and its mask copy [Bm, Hm, nq, nq].
+struct EtMask {
+  const int32_t* plan;
+  const uint8_t* mask;
+  int Bm, Hm, bs, causal;
+};
+
 // 4-D bf16 TMA map over [B, H, S, 64] with (b, h, s) element strides; box = rows x 64,
 // SWIZZLE_128B.  Defined in attn_fwd_tc.cu.
 int tc_make_map(CUtensorMap* map, const void* base, const int64_t st[3], int B, int H, int S, int rows);

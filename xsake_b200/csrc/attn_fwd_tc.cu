@@ -101,17 +101,6 @@ __device__ __forceinline__ void fail(volatile int* abort, int detail) {
   if (atomicExch((int*)abort, 1) == 0) record_device_error(DEV_ERR_TIMEOUT, detail);
 }
 
-// Warp-uniform wait for two barrier phases (the second only if `need2`, warp-uniform): both
-// probes go out before either result is used, so two satisfied waits cost about one.
-__device__ __forceinline__ bool warp_mbar_wait2(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2, bool need2,
-                                                volatile int* abort) {
-  const bool r1 = mbar_try_wait(b1, p1);
-  const bool r2 = need2 ? mbar_try_wait(b2, p2) : true;
-  bool ok = true;
-  if (!r1) ok = mbar_wait(b1, p1, abort);
-  if (ok && !r2) ok = mbar_wait(b2, p2, abort);
-  return __all_sync(0xffffffffu, ok);
-}
 
 // Mean over all S rows of V[b, h] for the rare fully-masked rows; one warp, no block sync.
 __device__ void warp_mean_v(const AttnArgs& a, int b, int h, float2& mine) {

@@ -253,6 +253,9 @@ int launch(const ProbsArgs& a, int D, cudaStream_t s) {
 }  // namespace
 
 int plan_layout_from_dims(const XsakeMaskDims* d, PlanLayout* L);
+size_t entropy_tc_split_bytes(int64_t batch, int64_t heads, int64_t seq);
+int entropy_tc(int dtype, const void* q, const void* k, const int64_t qs[3], const int64_t ks[3], int B, int H,
+               int S, float scale, double* partial, void* split_buf, cudaStream_t s, const EtMask* mask);
 
 }  // namespace xsake
 
@@ -297,6 +300,19 @@ int masked_args(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_d
 }  // namespace
 }  // namespace xsake
 
+namespace xsake {
+namespace {
+// Workspace: per-(b, h, 64-row tile) fp64 partials, then (from a 256-byte boundary) the bf16
+// parts of K the tensor-core kernel reads for fp32 inputs.
+size_t partial_bytes(int64_t batch, int64_t heads, int64_t seq) {
+  return (size_t)(batch * heads * ((seq + kRows - 1) / kRows)) * sizeof(double);
+}
+size_t split_offset(int64_t batch, int64_t heads, int64_t seq) {
+  return (partial_bytes(batch, heads, seq) + 255) / 256 * 256;
+}
+}  // namespace
+}  // namespace xsake
+
 extern "C" int xsake_attn_entropy(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
                                   const void* k_dev, double* head_sums_dev, void* workspace_dev,
                                   size_t workspace_bytes, void* stream) {
@@ -307,12 +323,19 @@ extern "C" int xsake_attn_entropy(const XsakeAttnDesc* desc, const void* plan_de
   XSAKE_REQUIRE(head_sums_dev != nullptr, XSAKE_EINVAL, "NULL argument");
   size_t need = 0;
   xsake_entropy_qk_workspace_size(a.B, a.H, a.S, &need);
-  XSAKE_REQUIRE(workspace_dev && workspace_bytes >= need, XSAKE_EINVAL, "workspace too small: %zu < %zu bytes",
-                workspace_bytes, need);
+  XSAKE_REQUIRE(workspace_dev && workspace_bytes >= need && ((uintptr_t)workspace_dev & 255) == 0, XSAKE_EINVAL,
+                "workspace must be %zu bytes, 256-byte aligned (got %zu bytes)", need, workspace_bytes);
   a.partial = reinterpret_cast<double*>(workspace_dev);
   cudaStream_t s = as_stream(stream);
-  int r = desc->dtype == XSAKE_F32 ? launch<float, kMaskedEntropy>(a, desc->head_dim, s)
-                                   : launch<__nv_bfloat16, kMaskedEntropy>(a, desc->head_dim, s);
+  int r;
+  if (desc->head_dim == 64) {
+    const EtMask mk{a.plan, a.mask, a.Bm, a.Hm, a.bs, a.causal};
+    void* split = reinterpret_cast<uint8_t*>(workspace_dev) + split_offset(a.B, a.H, a.S);
+    r = entropy_tc(desc->dtype, q_dev, k_dev, a.qs, a.ks, a.B, a.H, a.S, a.scale, a.partial, split, s, &mk);
+  } else {
+    r = desc->dtype == XSAKE_F32 ? launch<float, kMaskedEntropy>(a, desc->head_dim, s)
+                                 : launch<__nv_bfloat16, kMaskedEntropy>(a, desc->head_dim, s);
+  }
   if (r) return r;
   probs_heads_kernel<<<(unsigned)a.H, 256, 0, s>>>(a.partial, a.B, a.H, (a.S + kRows - 1) / kRows, head_sums_dev);
   return check_launch("probs_heads_kernel");
@@ -358,7 +381,7 @@ extern "C" int xsake_attn_probs(const XsakeAttnDesc* desc, const void* plan_dev,
 extern "C" int xsake_entropy_qk_workspace_size(int64_t batch, int64_t heads, int64_t seq, size_t* bytes) {
   clear_error();
   XSAKE_REQUIRE(bytes && batch > 0 && heads > 0 && seq > 0, XSAKE_EINVAL, "bad arguments");
-  *bytes = (size_t)(batch * heads * ((seq + kRows - 1) / kRows)) * sizeof(double);
+  *bytes = split_offset(batch, heads, seq) + entropy_tc_split_bytes(batch, heads, seq);
   return XSAKE_OK;
 }
 
@@ -372,8 +395,8 @@ extern "C" int xsake_entropy_qk(int32_t dtype, const void* q_dev, const void* k_
   XSAKE_REQUIRE(batch * heads < 65536 && seq < (1 << 30), XSAKE_EUNSUPPORTED, "too many (batch, head) slices");
   size_t need = 0;
   xsake_entropy_qk_workspace_size(batch, heads, seq, &need);
-  XSAKE_REQUIRE(workspace_dev && workspace_bytes >= need, XSAKE_EINVAL, "workspace too small: %zu < %zu bytes",
-                workspace_bytes, need);
+  XSAKE_REQUIRE(workspace_dev && workspace_bytes >= need && ((uintptr_t)workspace_dev & 255) == 0, XSAKE_EINVAL,
+                "workspace must be %zu bytes, 256-byte aligned (got %zu bytes)", need, workspace_bytes);
   ProbsArgs a{};
   a.q = q_dev;
   a.k = k_dev;
@@ -385,8 +408,15 @@ extern "C" int xsake_entropy_qk(int32_t dtype, const void* q_dev, const void* k_
   a.scale = scale > 0.f ? scale : 1.0f / sqrtf((float)head_dim);
   a.partial = reinterpret_cast<double*>(workspace_dev);
   cudaStream_t s = as_stream(stream);
-  int r = dtype == XSAKE_F32 ? launch<float, kEntropy>(a, (int)head_dim, s)
-                             : launch<__nv_bfloat16, kEntropy>(a, (int)head_dim, s);
+  int r;
+  if (head_dim == 64) {
+    // tensor cores (three bf16 parts per fp32 operand, see entropy_tc.cu)
+    void* split = reinterpret_cast<uint8_t*>(workspace_dev) + split_offset(batch, heads, seq);
+    r = entropy_tc(dtype, q_dev, k_dev, st, st, a.B, a.H, a.S, a.scale, a.partial, split, s, nullptr);
+  } else {
+    r = dtype == XSAKE_F32 ? launch<float, kEntropy>(a, (int)head_dim, s)
+                           : launch<__nv_bfloat16, kEntropy>(a, (int)head_dim, s);
+  }
   if (r) return r;
   probs_heads_kernel<<<(unsigned)heads, 256, 0, s>>>(a.partial, a.B, a.H, (a.S + kRows - 1) / kRows,
                                                      head_sums_dev);

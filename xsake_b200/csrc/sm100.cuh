@@ -69,6 +69,18 @@ __device__ __forceinline__ bool warp_mbar_wait(uint64_t* bar, uint32_t parity, v
   return __all_sync(0xffffffffu, ok);
 }
 
+// Warp-uniform wait for two barrier phases (the second only if `need2`, warp-uniform): both
+// probes go out before either result is used, so two satisfied waits cost about one.
+__device__ __forceinline__ bool warp_mbar_wait2(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2, bool need2,
+                                                volatile int* abort) {
+  const bool r1 = mbar_try_wait(b1, p1);
+  const bool r2 = need2 ? mbar_try_wait(b2, p2) : true;
+  bool ok = true;
+  if (!r1) ok = mbar_wait(b1, p1, abort);
+  if (ok && !r2) ok = mbar_wait(b2, p2, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // One lane of a converged warp (elect.sync): lets a whole warp run the uniform control flow
 // of a single-issuer role while exactly one lane issues the tcgen05 / TMA instructions.
 __device__ __forceinline__ bool elect_one() {
