@@ -161,9 +161,17 @@ XSAKE_API int xsake_attn_bwd(const XsakeAttnDesc* desc, const void* plan_dev, co
  * reference's calibration collects (training/trainer.py:79-117): p_dev (fp32, 16-byte aligned)
  * receives P[b, h, q, k] = softmax over all S keys of q.k * scale with masked entries at
  * finfo(float32).min, i.e. a fully masked row is uniform 1/S.  head_dim 32 or 64, fp32 or bf16
- * q/k through desc's strides; uses the plan's mask.  fp32 CUDA-core arithmetic. */
+ * q/k through desc's strides; uses the plan's mask.  Scores are fp32-accurate: bf16 inputs at
+ * head_dim 64 run on the tensor cores, everything else on the CUDA cores in fp32. */
 XSAKE_API int xsake_attn_probs(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
                    const void* k_dev, float* p_dev, void* stream);
+/* The same weights with a caller workspace (xsake_attn_probs_workspace_size bytes, 256-byte
+ * aligned), which lets fp32 inputs at head_dim 64 run on the tensor cores too (three bf16 parts
+ * per operand, as xsake_entropy_qk).  No counterpart in the reference beyond the weights. */
+XSAKE_API int xsake_attn_probs_workspace_size(const XsakeAttnDesc* desc, size_t* bytes);
+XSAKE_API int xsake_attn_probs_ex(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
+                   const void* k_dev, float* p_dev, void* workspace_dev, size_t workspace_bytes,
+                   void* stream);
 
 /* compute_attention_entropy (kernels/hads/hads_pattern.py:36-50) of exactly the weights
  * xsake_attn_probs gives (masked by the plan, causal cut, finfo.min fill), without materialising

@@ -63,6 +63,42 @@ def test_probs_batch_mask_head_dim_32_and_bf16():
     _probs_case(1, 2, 128, 64, 64, False, prof.block_masks, seed=530, dtype="bf16", scale=0.3)
 
 
+@pytest.mark.parametrize("dtype,bs,S,causal", [("f32", 32, 320, True), ("bf16", 64, 192, False),
+                                               ("f32", 30, 210, True)])
+def test_probs_entry_points_with_and_without_workspace(dtype, bs, S, causal):
+    # xsake_attn_probs (no workspace: tensor cores for bf16 at head_dim 64, CUDA cores for fp32)
+    # and xsake_attn_probs_ex (workspace: tensor cores for both) against the oracle's weights;
+    # S = 210 leaves rows that do not start on 16-byte boundaries (scalar stores) and a partial
+    # last 64-key chunk.
+    import ctypes as C
+    from xsake_b200 import sparse_attention as sa, _lib
+    B, H, D = 1, 2, 64
+    m = oh.dummy_hads_profile(H, S, bs, causal=causal, global_blocks=1).block_masks.copy()
+    m[1, 2, :] = False
+    q, k = _rand((B, H, S, D), 570), _rand((B, H, S, D), 571) * np.float32(1.5)
+    if dtype == "bf16":
+        q, k = (oi.to_bf16(x).astype(np.float32) for x in (q, k))
+    tdt = torch.float32 if dtype == "f32" else torch.bfloat16
+    tq, tk = (torch.from_numpy(x).to(tdt).cuda() for x in (q, k))
+    _, ref = oa.sparse_attention_reference(q, k, k, m, bs, causal=causal)
+    cm = sa.compile_block_mask(m, B, H, S, bs, causal, tq.device)
+    d = sa._desc(tq, tk, tk, tq, cm, None)
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    _lib.check(lib.xsake_attn_probs_workspace_size(C.byref(d), C.byref(n)))
+    ws = torch.empty(n.value, dtype=torch.uint8, device="cuda")
+    for with_ws in (False, True):
+        p = torch.full((B, H, S, S), float("nan"), device="cuda")
+        if with_ws:
+            _lib.check(lib.xsake_attn_probs_ex(C.byref(d), cm.plan.data_ptr(), tq.data_ptr(), tk.data_ptr(),
+                                               p.data_ptr(), ws.data_ptr(), ws.numel(), None))
+        else:
+            _lib.check(lib.xsake_attn_probs(C.byref(d), cm.plan.data_ptr(), tq.data_ptr(), tk.data_ptr(),
+                                            p.data_ptr(), None))
+        got = p.cpu().numpy()
+        assert np.abs(got - ref).max() <= P_TOL, (with_ws, np.abs(got - ref).max())
+
+
 def test_sparse_attention_use_pallas_false_returns_weights():
     from xsake_b200 import sparse_attention as sa
     prof = oh.dummy_hads_profile(2, 256, 64, causal=True)

@@ -79,6 +79,8 @@ _SIGS = {
     "xsake_entropy_rows": (C.c_int, [_VP, _I64, _I64, _I64, _I64, _VP, _VP, _SZ, _VP]),
     "xsake_entropy_rows_noalloc": (C.c_int, [_VP, _I64, _I64, _I64, _I64, _VP, _VP]),
     "xsake_attn_probs": (C.c_int, [C.POINTER(AttnDesc), _VP, _VP, _VP, _VP, _VP]),
+    "xsake_attn_probs_workspace_size": (C.c_int, [C.POINTER(AttnDesc), C.POINTER(_SZ)]),
+    "xsake_attn_probs_ex": (C.c_int, [C.POINTER(AttnDesc), _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "xsake_attn_entropy": (C.c_int, [C.POINTER(AttnDesc), _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "xsake_entropy_qk_workspace_size": (C.c_int, [_I64, _I64, _I64, C.POINTER(_SZ)]),
     "xsake_entropy_qk": (C.c_int, [_I32, _VP, _VP, _I64, _I64, _I64, _I64, _F, _VP, _VP, _SZ, _VP]),

@@ -255,7 +255,8 @@ int launch(const ProbsArgs& a, int D, cudaStream_t s) {
 int plan_layout_from_dims(const XsakeMaskDims* d, PlanLayout* L);
 size_t entropy_tc_split_bytes(int64_t batch, int64_t heads, int64_t seq);
 int entropy_tc(int dtype, const void* q, const void* k, const int64_t qs[3], const int64_t ks[3], int B, int H,
-               int S, float scale, double* partial, void* split_buf, cudaStream_t s, const EtMask* mask);
+               int S, float scale, double* partial, void* split_buf, cudaStream_t s, const EtMask* mask,
+               float* p_out);
 
 }  // namespace xsake
 
@@ -302,6 +303,14 @@ int masked_args(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_d
 
 namespace xsake {
 namespace {
+// Rows the tensor-core kernel reads with 16-byte loads / TMA: base and (b, h, s) strides aligned.
+bool tc_rows_aligned(int dtype, const void* q, const void* k, const int64_t qs[3], const int64_t ks[3]) {
+  const int64_t al = dtype == XSAKE_F32 ? 4 : 8;
+  bool ok = ((uintptr_t)q & 15) == 0 && ((uintptr_t)k & 15) == 0;
+  for (int i = 0; i < 3; ++i) ok = ok && qs[i] % al == 0 && ks[i] % al == 0;
+  return ok;
+}
+
 // Workspace: per-(b, h, 64-row tile) fp64 partials, then (from a 256-byte boundary) the bf16
 // parts of K the tensor-core kernel reads for fp32 inputs.
 size_t partial_bytes(int64_t batch, int64_t heads, int64_t seq) {
@@ -328,10 +337,10 @@ extern "C" int xsake_attn_entropy(const XsakeAttnDesc* desc, const void* plan_de
   a.partial = reinterpret_cast<double*>(workspace_dev);
   cudaStream_t s = as_stream(stream);
   int r;
-  if (desc->head_dim == 64) {
+  if (desc->head_dim == 64 && tc_rows_aligned(desc->dtype, q_dev, k_dev, a.qs, a.ks)) {
     const EtMask mk{a.plan, a.mask, a.Bm, a.Hm, a.bs, a.causal};
     void* split = reinterpret_cast<uint8_t*>(workspace_dev) + split_offset(a.B, a.H, a.S);
-    r = entropy_tc(desc->dtype, q_dev, k_dev, a.qs, a.ks, a.B, a.H, a.S, a.scale, a.partial, split, s, &mk);
+    r = entropy_tc(desc->dtype, q_dev, k_dev, a.qs, a.ks, a.B, a.H, a.S, a.scale, a.partial, split, s, &mk, nullptr);
   } else {
     r = desc->dtype == XSAKE_F32 ? launch<float, kMaskedEntropy>(a, desc->head_dim, s)
                                  : launch<__nv_bfloat16, kMaskedEntropy>(a, desc->head_dim, s);
@@ -341,41 +350,56 @@ extern "C" int xsake_attn_entropy(const XsakeAttnDesc* desc, const void* plan_de
   return check_launch("probs_heads_kernel");
 }
 
+namespace xsake {
+namespace {
+// xsake_attn_probs(_ex): tensor cores at head_dim 64 when the inputs are bf16 or a workspace for
+// the bf16 parts of fp32 K is given, CUDA cores otherwise.
+int probs_impl(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev, const void* k_dev, float* p_dev,
+               void* ws, size_t ws_bytes, void* stream) {
+  XSAKE_REQUIRE(p_dev != nullptr, XSAKE_EINVAL, "NULL argument");
+  ProbsArgs a;
+  int st = masked_args(desc, plan_dev, q_dev, k_dev, &a);
+  if (st) return st;
+  XSAKE_REQUIRE(((uintptr_t)p_dev & 15) == 0, XSAKE_EINVAL, "p must be 16-byte aligned");
+  a.p = p_dev;
+  cudaStream_t s = as_stream(stream);
+  const bool f32 = desc->dtype == XSAKE_F32;
+  const size_t split = f32 ? entropy_tc_split_bytes(a.B, a.H, a.S) : 0;
+  const bool have_ws = !f32 || (ws && ws_bytes >= split && ((uintptr_t)ws & 255) == 0);
+  if (desc->head_dim == 64 && have_ws && tc_rows_aligned(desc->dtype, q_dev, k_dev, a.qs, a.ks)) {
+    const EtMask mk{a.plan, a.mask, a.Bm, a.Hm, a.bs, a.causal};
+    return entropy_tc(desc->dtype, q_dev, k_dev, a.qs, a.ks, a.B, a.H, a.S, a.scale, nullptr, f32 ? ws : nullptr, s,
+                      &mk, p_dev);
+  }
+  return f32 ? launch<float, kProbs>(a, desc->head_dim, s) : launch<__nv_bfloat16, kProbs>(a, desc->head_dim, s);
+}
+}  // namespace
+}  // namespace xsake
+
 extern "C" int xsake_attn_probs(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
                                 const void* k_dev, float* p_dev, void* stream) {
   clear_error();
-  XSAKE_REQUIRE(desc && plan_dev && q_dev && k_dev && p_dev, XSAKE_EINVAL, "NULL argument");
-  XSAKE_REQUIRE(desc->dtype == XSAKE_F32 || desc->dtype == XSAKE_BF16, XSAKE_EINVAL, "dtype %d", desc->dtype);
-  XSAKE_REQUIRE(desc->batch > 0 && desc->heads > 0 && desc->seq > 0, XSAKE_EINVAL, "dims must be positive");
-  XsakeMaskDims md{desc->batch, desc->heads, desc->seq, desc->mask_batch, desc->mask_heads, desc->block_size,
-                   desc->causal};
-  PlanLayout L;
-  int st = plan_layout_from_dims(&md, &L);
+  return probs_impl(desc, plan_dev, q_dev, k_dev, p_dev, nullptr, 0, stream);
+}
+
+extern "C" int xsake_attn_probs_workspace_size(const XsakeAttnDesc* desc, size_t* bytes) {
+  clear_error();
+  XSAKE_REQUIRE(desc && bytes && desc->batch > 0 && desc->heads > 0 && desc->seq > 0, XSAKE_EINVAL, "bad arguments");
+  *bytes = std::max<size_t>(256, entropy_tc_split_bytes(desc->batch, desc->heads, desc->seq));
+  return XSAKE_OK;
+}
+
+extern "C" int xsake_attn_probs_ex(const XsakeAttnDesc* desc, const void* plan_dev, const void* q_dev,
+                                   const void* k_dev, float* p_dev, void* workspace_dev, size_t workspace_bytes,
+                                   void* stream) {
+  clear_error();
+  XSAKE_REQUIRE(desc != nullptr, XSAKE_EINVAL, "NULL argument");
+  size_t need = 0;
+  int st = xsake_attn_probs_workspace_size(desc, &need);
   if (st) return st;
-  XSAKE_REQUIRE(((uintptr_t)p_dev & 15) == 0 && ((uintptr_t)plan_dev & 15) == 0, XSAKE_EINVAL,
-                "p and plan must be 16-byte aligned");
-  XSAKE_REQUIRE((int64_t)desc->batch * desc->heads < 65536, XSAKE_EUNSUPPORTED, "too many (batch, head) slices");
-  ProbsArgs a{};
-  a.q = q_dev;
-  a.k = k_dev;
-  for (int i = 0; i < 3; ++i) {
-    a.qs[i] = desc->q_stride[i];
-    a.ks[i] = desc->k_stride[i];
-  }
-  a.B = desc->batch;
-  a.H = desc->heads;
-  a.S = desc->seq;
-  a.scale = desc->scale > 0.f ? desc->scale : 1.0f / sqrtf((float)desc->head_dim);
-  a.causal = desc->causal ? 1 : 0;
-  a.plan = reinterpret_cast<const int32_t*>(plan_dev);
-  a.mask = reinterpret_cast<const uint8_t*>(a.plan + L.mask_off);
-  a.Bm = L.Bm;
-  a.Hm = L.Hm;
-  a.bs = L.bs;
-  a.p = p_dev;
-  cudaStream_t s = as_stream(stream);
-  return desc->dtype == XSAKE_F32 ? launch<float, kProbs>(a, desc->head_dim, s)
-                                  : launch<__nv_bfloat16, kProbs>(a, desc->head_dim, s);
+  XSAKE_REQUIRE(workspace_dev && workspace_bytes >= need && ((uintptr_t)workspace_dev & 255) == 0, XSAKE_EINVAL,
+                "workspace must be %zu bytes, 256-byte aligned (got %zu bytes)", need, workspace_bytes);
+  return probs_impl(desc, plan_dev, q_dev, k_dev, p_dev, workspace_dev, workspace_bytes, stream);
 }
 
 extern "C" int xsake_entropy_qk_workspace_size(int64_t batch, int64_t heads, int64_t seq, size_t* bytes) {
@@ -412,7 +436,7 @@ extern "C" int xsake_entropy_qk(int32_t dtype, const void* q_dev, const void* k_
   if (head_dim == 64) {
     // tensor cores (three bf16 parts per fp32 operand, see entropy_tc.cu)
     void* split = reinterpret_cast<uint8_t*>(workspace_dev) + split_offset(batch, heads, seq);
-    r = entropy_tc(dtype, q_dev, k_dev, st, st, a.B, a.H, a.S, a.scale, a.partial, split, s, nullptr);
+    r = entropy_tc(dtype, q_dev, k_dev, st, st, a.B, a.H, a.S, a.scale, a.partial, split, s, nullptr, nullptr);
   } else {
     r = dtype == XSAKE_F32 ? launch<float, kEntropy>(a, (int)head_dim, s)
                            : launch<__nv_bfloat16, kEntropy>(a, (int)head_dim, s);

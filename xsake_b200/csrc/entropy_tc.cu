@@ -69,7 +69,8 @@ struct EtParams {
   int q_fp32;              // Q element type
   int k_split;             // 1: K parts in the split buffer [3][B*H][S64][64]; 0: K is the bf16 input
   float scale_log2;        // scale * log2(e)
-  double* partial;         // [B * H * ceil(S / 64)]
+  double* partial;         // entropy: [B * H * ceil(S / 64)]
+  float* p_out;            // weights: [B, H, S, S] fp32
   // masked weights (xsake_attn_entropy): the plan's mask copy [Bm, Hm, nq, nq] and the causal cut
   int masked;
   const int32_t* plan;
@@ -150,6 +151,10 @@ __device__ __forceinline__ void split_words(const float* v, uint32_t (&w1)[NW], 
   }
 }
 
+// MODE kEtEntropy: per-tile entropy partials; kEtProbs: the weights themselves (pass 2 writes p).
+constexpr int kEtEntropy = 0, kEtProbs = 1;
+
+template <int MODE>
 __global__ void __launch_bounds__(kEtThreads, 2)
 entropy_tc_kernel(const __grid_constant__ CUtensorMap tmK, const EtParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -197,7 +202,7 @@ entropy_tc_kernel(const __grid_constant__ CUtensorMap tmK, const EtParams p) {
   const uint32_t tmem = *tmem_slot;
 
   if (!*plan_ok) {
-    if (threadIdx.x < 128 && (threadIdx.x & 63) == 0 && 2 * (int)blockIdx.x + (int)(threadIdx.x >> 6) < nk)
+    if (MODE == kEtEntropy && threadIdx.x < 128 && (threadIdx.x & 63) == 0 && 2 * (int)blockIdx.x + (int)(threadIdx.x >> 6) < nk)
       p.partial[(int64_t)bh * nk + 2 * blockIdx.x + (threadIdx.x >> 6)] = (double)NAN;
   } else if (warp == 4) {
     // ------------------------------------------------------------------ K producer
@@ -352,6 +357,27 @@ entropy_tc_kernel(const __grid_constant__ CUtensorMap tmK, const EtParams p) {
       }
       return a0 + a1;
     };
+    // Pass-2 weights of one chunk of this row: p = 2^(x - m) / l for its keys < lim, written
+    // 16 bytes at a time when rows start on 16-byte boundaries.
+    auto store_probs = [&](const float* x, int lim, int chunk) {
+      float* dst = p.p_out + ((int64_t)bh * p.S + tok) * p.S + 64 * chunk;
+      const uint64_t nm = pk2(-m, -m), il = pk2(inv_l, inv_l);
+      if (lim >= 64 && (p.S & 3) == 0) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float d0, d1, d2, d3, p0, p1, p2, p3;
+          upk2(add2(pk2(x[4 * j], x[4 * j + 1]), nm), d0, d1);
+          upk2(add2(pk2(x[4 * j + 2], x[4 * j + 3]), nm), d2, d3);
+          upk2(mul2(pk2(ex2(d0), ex2(d1)), il), p0, p1);
+          upk2(mul2(pk2(ex2(d2), ex2(d3)), il), p2, p3);
+          reinterpret_cast<float4*>(dst)[j] = make_float4(p0, p1, p2, p3);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 64; ++j)
+          if (j < lim) dst[j] = ex2(x[j] - m) * inv_l;
+      }
+    };
     for (int t = 0; t < nsteps; ++t) {
       const int buf = t & 1;
       if (!warp_mbar_wait(&bars->s_full[buf], (t >> 1) & 1, abort)) { ok = false; break; }
@@ -396,6 +422,8 @@ entropy_tc_kernel(const __grid_constant__ CUtensorMap tmK, const EtParams p) {
           inv_l = 1.f / l;
           lg2l = log2f(l);
         }
+      } else if (MODE == kEtProbs) {
+        if (valid) store_probs(x, lim, chunk);
       } else {
         ent += lim < 64 ? terms(x, lim, true) : terms(x, 64, false);
       }
@@ -403,7 +431,7 @@ entropy_tc_kernel(const __grid_constant__ CUtensorMap tmK, const EtParams p) {
     // Row entropy H = -ln 2 * sum c log2 c; each 64-row half sums its rows in order in fp64.
     s_row[r] = !ok ? (double)NAN : valid ? -(double)(ent * kLn2) : 0.0;
     named_bar_sync(1, 128);
-    if ((r & 63) == 0) {
+    if (MODE == kEtEntropy && (r & 63) == 0) {
       double acc = 0.0;
       for (int i = r; i < r + 64; ++i) acc += s_row[i];
       const int tile = 2 * blockIdx.x + (r >> 6);
@@ -424,6 +452,14 @@ constexpr int kEtMaxDev = 64;
 std::once_flag g_et_attr_once[kEtMaxDev];
 cudaError_t g_et_attr_err[kEtMaxDev];
 
+cudaError_t et_set_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(entropy_tc_kernel<kEtEntropy>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kEtSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(entropy_tc_kernel<kEtProbs>, cudaFuncAttributeMaxDynamicSharedMemorySize, kEtSmemBytes);
+  return e;
+}
+
 }  // namespace
 
 size_t entropy_tc_split_bytes(int64_t batch, int64_t heads, int64_t seq) {
@@ -431,10 +467,11 @@ size_t entropy_tc_split_bytes(int64_t batch, int64_t heads, int64_t seq) {
 }
 
 // Launches the split (fp32 inputs) and the entropy kernel (of the masked weights when mask is
-// given); partial = [B * H * ceil(S / 64)] doubles,
+// given; writing the weights themselves to p_out instead when p_out is given); partial = [B * H * ceil(S / 64)] doubles,
 // split_buf (fp32 inputs) = entropy_tc_split_bytes(B, H, S) bytes, 256-byte aligned.
 int entropy_tc(int dtype, const void* q, const void* k, const int64_t qs[3], const int64_t ks[3], int B, int H,
-               int S, float scale, double* partial, void* split_buf, cudaStream_t s, const EtMask* mask) {
+               int S, float scale, double* partial, void* split_buf, cudaStream_t s, const EtMask* mask,
+               float* p_out) {
   DeviceInfo di;
   int st = device_info(&di);
   if (st) return st;
@@ -462,10 +499,7 @@ int entropy_tc(int dtype, const void* q, const void* k, const int64_t qs[3], con
   int dev = 0;
   XSAKE_CUDA_TRY(cudaGetDevice(&dev));
   XSAKE_REQUIRE(dev < kEtMaxDev, XSAKE_EUNSUPPORTED, "device ordinal %d", dev);
-  std::call_once(g_et_attr_once[dev], [dev] {
-    g_et_attr_err[dev] = cudaFuncSetAttribute(entropy_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              kEtSmemBytes);
-  });
+  std::call_once(g_et_attr_once[dev], [dev] { g_et_attr_err[dev] = et_set_attributes(); });
   XSAKE_REQUIRE(g_et_attr_err[dev] == cudaSuccess, XSAKE_ECUDA, "cudaFuncSetAttribute: %s",
                 cudaGetErrorString(g_et_attr_err[dev]));
   EtParams p{};
@@ -488,9 +522,15 @@ int entropy_tc(int dtype, const void* q, const void* k, const int64_t qs[3], con
     p.bs = mask->bs;
     p.causal = mask->causal;
   }
+  p.p_out = p_out;
   dim3 grid((S + 127) / 128, B * H);
-  entropy_tc_kernel<<<grid, kEtThreads, kEtSmemBytes, s>>>(mk, p);
-  return check_launch("entropy_tc_kernel");
+  if (p_out) {
+    XSAKE_REQUIRE(((uintptr_t)p_out & 15) == 0, XSAKE_EINVAL, "p must be 16-byte aligned");
+    entropy_tc_kernel<kEtProbs><<<grid, kEtThreads, kEtSmemBytes, s>>>(mk, p);
+  } else {
+    entropy_tc_kernel<kEtEntropy><<<grid, kEtThreads, kEtSmemBytes, s>>>(mk, p);
+  }
+  return check_launch(p_out ? "entropy_tc_kernel (weights)" : "entropy_tc_kernel");
 }
 
 }  // namespace xsake

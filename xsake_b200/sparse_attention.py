@@ -391,8 +391,9 @@ def attention_probabilities(q, k, block_mask, block_size: int = 128, scale: Opti
                             causal: bool = False):
     """The attention weights of ``sparse_attention_reference`` (sparse_attention.py:45-91):
     fp32 [B, H, S, S] softmax over all S keys of ``q k^T * scale`` with masked entries at
-    finfo(float32).min (a fully masked row is uniform).  Computed on the GPU (fp32 CUDA-core
-    scores); NumPy in, NumPy out, CUDA tensor in, CUDA tensor out."""
+    finfo(float32).min (a fully masked row is uniform).  Computed on the GPU with fp32-accurate
+    scores (tensor cores at d_head 64, CUDA cores otherwise); NumPy in, NumPy out, CUDA tensor
+    in, CUDA tensor out."""
     was_host = not (isinstance(q, torch.Tensor) and q.is_cuda)
     q, k = (_unit_last(dev.to_device(t)[0]) for t in (q, k))
     if q.dim() != 4 or k.shape != q.shape or k.dtype != q.dtype:
@@ -402,8 +403,12 @@ def attention_probabilities(q, k, block_mask, block_size: int = 128, scale: Opti
     cm = compile_block_mask(block_mask, B, H, S, block_size, causal, q.device)
     p = torch.empty((B, H, S, S), dtype=torch.float32, device=q.device)
     d = _desc(q, k, k, q, cm, scale)
-    _lib.check(_lib.load().xsake_attn_probs(C.byref(d), cm.plan.data_ptr(), q.data_ptr(), k.data_ptr(),
-                                            p.data_ptr(), dev.stream_ptr()))
+    lib = _lib.load()
+    n = C.c_size_t(0)
+    _lib.check(lib.xsake_attn_probs_workspace_size(C.byref(d), C.byref(n)))
+    ws = dev.workspace(n.value, q.device)
+    _lib.check(lib.xsake_attn_probs_ex(C.byref(d), cm.plan.data_ptr(), q.data_ptr(), k.data_ptr(), p.data_ptr(),
+                                       ws.data_ptr(), ws.numel(), dev.stream_ptr()))
     return dev.to_host(p) if was_host else p
 
 
