@@ -879,18 +879,44 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       ++pvs;
       return true;
     };
-    for (uint32_t k = 0; ok; ++k) {
-      const int slot = k & 1;
-      if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
-      const int item = item_slot[slot];
+    // Taking an item reads its work entry, its step count and its first 32 entries (dependent
+    // global loads).  The next item is taken while this item's last PVs wait for their P, when the
+    // scheduler has already published it, so its first QK follows the last PV directly.
+    struct Taken {
+      int item, cnt, last;
+      PItem w;
+      int32_t held;   // entries [0, 32) of the item, lane j holding entry j
+    };
+    auto take = [&](uint32_t kk, Taken& t) -> bool {
+      const int slot = kk & 1;
+      if (!warp_mbar_wait(&bars->item_full[X][slot], (kk >> 1) & 1, abort)) return false;
+      t.item = item_slot[slot];
       __syncwarp();
       if (elect_one()) mbar_arrive(&bars->item_empty[X][slot]);
       __syncwarp();
-      if (item < 0) break;
-      const PItem w = decode_pair(a, item);
+      t.cnt = 0;
+      if (t.item >= 0) {
+        t.w = decode_pair(a, t.item);
+        t.cnt = count_steps(entries, t.w.e0, t.w.n, (t.w.j & 1) ? kFlagActive1 : kFlagActive0, t.last);
+        t.held = lane < t.w.n ? entries[t.w.e0 + lane] : 0;
+      }
+      return true;
+    };
+    Taken cur, nxt;
+    bool have_next = false;
+    for (uint32_t k = 0; ok; ++k) {
+      if (have_next) {
+        cur = nxt;
+        have_next = false;
+      } else if (!take(k, cur)) {
+        ok = false;
+        break;
+      }
+      if (cur.item < 0) break;
+      if (cur.cnt == 0) continue;
+      const PItem& w = cur.w;
       const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
-      int last_used = -1;
-      if (count_steps(entries, w.e0, w.n, fa, last_used) == 0) continue;
+      const int last_used = cur.last;
       const int qs = qk % kQSlots;
       if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
       ++qk;
@@ -898,8 +924,8 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       const uint64_t qda = sw128_desc(qaddr, 16, 1024), qdb = sw128_desc(qaddr + kQBytes / 2, 16, 1024);
       item_first = steps;
       solo = w.solo;
-      int32_t held = 0;
-      int base = -32;
+      int32_t held = cur.held;
+      int base = 0;
       for (int i = 0; i < w.n && ok; ++i) {
         const int32_t e = entry_at(entries, w, i, held, base);
         if (!(e & fa)) continue;
@@ -937,6 +963,10 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
         ++steps;
       }
       if (!ok) break;
+      if (__all_sync(0xffffffffu, mbar_test_wait(&bars->item_full[X][(k + 1) & 1], ((k + 1) >> 1) & 1))) {
+        if (!take(k + 1, nxt)) { ok = false; break; }
+        have_next = true;
+      }
       while (ok && pvs < steps) ok = issue_pv();
       if (!ok) break;
       if (steps > item_first) ++titems;
@@ -966,13 +996,33 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
     bool s_ready = false;
     uint32_t ep_phase = 0;                 // uses of ep_bar[X]
     bool ok = true;
+    // The next item's id, work entry and first 32 entries are read before this item's epilogue
+    // when the scheduler has already published it (the reads overlap the wait for the last PV).
+    int n_item = -1;
+    int32_t n_wk = 0, n_eb = 0;
+    bool have_next = false;
+    auto entries0 = [&](int32_t wkx) {
+      const int e0 = work_word(wkx, 3), n = work_word(wkx, 4) - e0;
+      return lane < n ? entries[e0 + lane] : 0;
+    };
     for (uint32_t k = 0; ok; ++k) {
-      const int slot = k & 1;
-      if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
-      const int item = item_slot[slot];
-      mbar_arrive(&bars->item_empty[X][slot]);
+      int item;
+      int32_t wk, eb0;
+      if (have_next) {
+        item = n_item;
+        wk = n_wk;
+        eb0 = n_eb;
+        have_next = false;
+      } else {
+        const int slot = k & 1;
+        if (!warp_mbar_wait(&bars->item_full[X][slot], (k >> 1) & 1, abort)) { ok = false; break; }
+        item = item_slot[slot];
+        mbar_arrive(&bars->item_empty[X][slot]);
+        if (item < 0) break;
+        wk = work_lanes(a, item);
+        eb0 = entries0(wk);
+      }
       if (item < 0) break;
-      const int32_t wk = work_lanes(a, item);
       const int we0 = work_word(wk, 3), wn = work_word(wk, 4) - we0, wj = work_word(wk, 2);
       const int32_t fa = (wj & 1) ? kFlagActive1 : kFlagActive0;
       const int32_t fd = (wj & 1) ? kFlagDiag1 : kFlagDiag0;
@@ -980,7 +1030,7 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       float m = -INFINITY, l = 0.f;
       int nsteps = 0;
       for (int b0 = 0; b0 < wn && ok; b0 += 32) {
-        const int32_t eb = b0 + lane < wn ? entries[we0 + b0 + lane] : 0;
+        const int32_t eb = b0 == 0 ? eb0 : (b0 + lane < wn ? entries[we0 + b0 + lane] : 0);
         uint32_t own = __ballot_sync(0xffffffffu, (eb & fa) != 0);
         while (own) {
           const int32_t e = __shfl_sync(0xffffffffu, eb, __ffs(own) - 1);
@@ -1060,6 +1110,15 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
         }
       }
       if (!ok) break;
+      if (__all_sync(0xffffffffu, mbar_test_wait(&bars->item_full[X][(k + 1) & 1], ((k + 1) >> 1) & 1))) {
+        n_item = item_slot[(k + 1) & 1];
+        mbar_arrive(&bars->item_empty[X][(k + 1) & 1]);
+        if (n_item >= 0) {
+          n_wk = work_lanes(a, n_item);
+          n_eb = entries0(n_wk);
+        }
+        have_next = true;
+      }
       // ---------------------------------------------------------------- epilogue
       float o[64];
       if (nsteps > 0) {
