@@ -1094,11 +1094,14 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
             acc[j & 3] = add2(acc[j & 3], pk2(p0, p1));
             __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
             pk[j] = *reinterpret_cast<uint32_t*>(&pb);
+            // The first 16 columns of P go out while the second half is computed, so only the
+            // second store's latency is left before the arrive (A/B: ~1%, identical outputs).
+            if (j == 15) XSAKE_TMEM_ST16(tcol + lane_base + 64 * sb, pk);
           }
           float s0, s1;
           upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])), s0, s1);
           l += s0 + s1;
-          XSAKE_TMEM_ST32(tcol + lane_base + 64 * sb, pk);
+          XSAKE_TMEM_ST16(tcol + lane_base + 64 * sb + 16, (pk + 16));
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(&p_full[sb]);
