@@ -386,17 +386,6 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             const float4* dl4 = nl4 + 16;
             if (!warp_mbar_wait(&bars->s_full, g & 1, abort)) { ok = false; break; }
             tc_fence_after();
-            uint32_t sr[64], dr[64];
-            XSAKE_TMEM_LD32(tmem + lane_base + 0, sr);
-            XSAKE_TMEM_LD32(tmem + lane_base + 32, (sr + 32));
-            XSAKE_TMEM_LD32(tmem + lane_base + 64, dr);
-            XSAKE_TMEM_LD32(tmem + lane_base + 96, (dr + 32));
-            XSAKE_TMEM_WAIT_LD32(sr);
-            XSAKE_TMEM_WAIT_LD32((sr + 32));
-            XSAKE_TMEM_WAIT_LD32(dr);
-            XSAKE_TMEM_WAIT_LD32((dr + 32));
-            tc_fence_before();
-            mbar_arrive(&bars->s_free);
             // The chunk's -lse*log2e and Dl came with its TMA copies.
             if (!warp_mbar_wait(&bars->ring_full[st], (g / kKvStages) & 1, abort)) { ok = false; break; }
             const bool act = (e & f_active) != 0;    // warp-uniform (a warp is inside one half)
@@ -406,20 +395,30 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             for (int hh = 0; hh < 2; ++hh) {
               uint32_t* pp = ppa[hh];
               uint32_t* pd = pda[hh];
+              uint32_t sr[32], dr[32];   // half hh of S^T and dP^T: 64 registers live instead of 128
+              XSAKE_TMEM_LD32(tmem + lane_base + 32 * hh, sr);
+              XSAKE_TMEM_LD32(tmem + lane_base + 64 + 32 * hh, dr);
+              XSAKE_TMEM_WAIT_LD32(sr);
+              XSAKE_TMEM_WAIT_LD32(dr);
+              if (hh == 1) {
+                tc_fence_before();
+                mbar_arrive(&bars->s_free);
+              }
               if (act) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
                   const float4 nl = nl4[8 * hh + q], dl = dl4[8 * hh + q];
-                  const int j0 = 32 * hh + 4 * q;
+                  const int jq = 32 * hh + 4 * q;   // query index within the chunk
+                  const int j0 = 4 * q;             // index within this half's registers
                   float x0, x1, x2, x3;
                   upk2(fma2(pk2(__uint_as_float(sr[j0]), __uint_as_float(sr[j0 + 1])), cc2, pk2(nl.x, nl.y)), x0, x1);
                   upk2(fma2(pk2(__uint_as_float(sr[j0 + 2]), __uint_as_float(sr[j0 + 3])), cc2, pk2(nl.z, nl.w)), x2, x3);
                   float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
                   if (dg) {   // token-level causal cut: key kl is after query j
-                    if (j0 < kl) p0 = 0.f;
-                    if (j0 + 1 < kl) p1 = 0.f;
-                    if (j0 + 2 < kl) p2 = 0.f;
-                    if (j0 + 3 < kl) p3 = 0.f;
+                    if (jq < kl) p0 = 0.f;
+                    if (jq + 1 < kl) p1 = 0.f;
+                    if (jq + 2 < kl) p2 = 0.f;
+                    if (jq + 3 < kl) p3 = 0.f;
                   }
                   float d0, d1, d2, d3;
                   upk2(mul2(pk2(p0, p1), sub2(pk2(__uint_as_float(dr[j0]), __uint_as_float(dr[j0 + 1])), pk2(dl.x, dl.y))), d0, d1);
@@ -675,33 +674,32 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
             const int32_t e = entries[w.e0 + i];
             if (!warp_mbar_wait(&bars->s_full, g & 1, abort)) { ok = false; break; }
             tc_fence_after();
-            uint32_t sr[64], dr[64];
-            XSAKE_TMEM_LD32(tmem + lane_base + 0, sr);
-            XSAKE_TMEM_LD32(tmem + lane_base + 32, (sr + 32));
-            XSAKE_TMEM_LD32(tmem + lane_base + 64, dr);
-            XSAKE_TMEM_LD32(tmem + lane_base + 96, (dr + 32));
-            XSAKE_TMEM_WAIT_LD32(sr);
-            XSAKE_TMEM_WAIT_LD32((sr + 32));
-            XSAKE_TMEM_WAIT_LD32(dr);
-            XSAKE_TMEM_WAIT_LD32((dr + 32));
-            tc_fence_before();
-            mbar_arrive(&bars->s_free);
             const bool act = (e & f_active) != 0;    // warp-uniform
             const bool dg = (e & f_diag) != 0;
             uint32_t pda[2][16];   // dS of this row, bf16 pairs
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
               uint32_t* pd = pda[hh];
+              uint32_t sr[32], dr[32];   // half hh of S and dP: 64 registers live instead of 128
+              XSAKE_TMEM_LD32(tmem + lane_base + 32 * hh, sr);
+              XSAKE_TMEM_LD32(tmem + lane_base + 64 + 32 * hh, dr);
+              XSAKE_TMEM_WAIT_LD32(sr);
+              XSAKE_TMEM_WAIT_LD32(dr);
+              if (hh == 1) {
+                tc_fence_before();
+                mbar_arrive(&bars->s_free);
+              }
               if (act) {
 #pragma unroll
                 for (int q = 0; q < 16; ++q) {
-                  const int j0 = 32 * hh + 2 * q;
+                  const int jk = 32 * hh + 2 * q;   // key index within the chunk
+                  const int j0 = 2 * q;             // index within this half's registers
                   float x0, x1;
                   upk2(fma2(pk2(__uint_as_float(sr[j0]), __uint_as_float(sr[j0 + 1])), cc2, nl2), x0, x1);
                   float p0 = ex2(x0), p1 = ex2(x1);
                   if (dg) {   // token-level causal cut: key j is after query ql
-                    if (j0 > ql) p0 = 0.f;
-                    if (j0 + 1 > ql) p1 = 0.f;
+                    if (jk > ql) p0 = 0.f;
+                    if (jk + 1 > ql) p1 = 0.f;
                   }
                   float d0, d1;
                   upk2(mul2(pk2(p0, p1), sub2(pk2(__uint_as_float(dr[j0]), __uint_as_float(dr[j0 + 1])), dl2)), d0, d1);
