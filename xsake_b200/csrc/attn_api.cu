@@ -81,10 +81,10 @@ extern "C" int xsake_attn_bwd_workspace_size(const XsakeAttnDesc* desc, size_t* 
   clear_error();
   XSAKE_REQUIRE(desc && bytes, XSAKE_EINVAL, "NULL argument");
   const int64_t bh = (int64_t)desc->batch * desc->heads;
-  // delta [B*H*S] | ucol [B*H*D] | -lse*log2e [B*H*S] | work-item counters; the CUDA-core
-  // backward uses the first two sections.
+  // delta [B*H*S] | ucol [B*H*D] | -lse*log2e [B*H*S] | work-item counters | 32 bytes per query
+  // row of bias operands (tensor-core backward); the CUDA-core backward uses the first two sections.
   const size_t rows = align_up((size_t)(bh * desc->seq) * 4, 256);
-  *bytes = 2 * rows + align_up((size_t)(bh * desc->head_dim) * 4, 256) + 256;
+  *bytes = 2 * rows + align_up((size_t)(bh * desc->head_dim) * 4, 256) + 256 + (size_t)(bh * desc->seq) * 32;
   return XSAKE_OK;
 }
 

@@ -49,10 +49,19 @@ constexpr uint32_t kIdescAcc = idesc_bf16(128, 64, true);   // B MN-major (rows 
 constexpr int kItemReaders = 1 + 128;                       // MMA warp + elementwise threads
 
 // ---- dK/dV kernel shared memory
+// The per-query terms of P^T and dS^T enter through the tensor core: each chunk carries a bias
+// operand of 64 query rows x 16 bf16 (SWIZZLE_32B) holding three bf16 parts of -lse/scale
+// (elements 0-2) and of -Dl (elements 3-5), and two constant selector blocks of 128 key rows
+// (ones at elements 0-2, resp. 3-5) turn one extra K=16 MMA per product into
+// S^T + (-lse/scale) and dP^T - Dl, so the elementwise threads read no per-query values.
 constexpr int kKvStages = 2;
-constexpr int kKvStageBytes = 2 * kChunkBytes + 1024;       // Q, dO, -lse*log2e [64], Dl [64], pad
+constexpr int kBiasBytes = 64 * 32;                         // bias operand of one 64-query chunk
+constexpr int kSelBytes = 128 * 32;                         // one selector block
+constexpr int kKvStageBytes = 2 * kChunkBytes + kBiasBytes; // Q, dO, bias (1024-byte multiple)
 constexpr int kOffK = 0, kOffV = kTileBytes, kOffPt = 2 * kTileBytes, kOffDSt = 3 * kTileBytes;
-constexpr int kOffKvRing = 4 * kTileBytes;
+constexpr int kOffSel = 4 * kTileBytes;                     // selectors of the lse and Dl parts
+constexpr int kOffKvRing = kOffSel + 2 * kSelBytes;
+static_assert(kKvStageBytes % 1024 == 0 && kOffKvRing % 1024 == 0, "SWIZZLE_128B stage alignment");
 constexpr int kOffKvBar = kOffKvRing + kKvStages * kKvStageBytes;
 
 // ---- dQ kernel shared memory
@@ -81,6 +90,7 @@ struct BwdParams {
   AttnArgs a;
   float scale_log2;     // scale * log2(e)
   const float* nlse2;   // [B*H*S] -lse * log2(e); -inf for fully masked rows
+  const uint8_t* bias;  // [B*H][S/64] bias operands of kBiasBytes (written by the prep kernel)
   int* counter;         // two work-item counters, zeroed by the host before the launches
 };
 
@@ -229,6 +239,18 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
     if (!*plan_ok) record_device_error(DEV_ERR_PLAN, 20);
     init_bars(bars);
   }
+  if (threadIdx.x < 128) {
+    // Selector rows, the same for every key row: bf16 1.0 at elements 0-2 (first block) and 3-5.
+    constexpr uint32_t kOne = 0x3F80u;
+    const int r = threadIdx.x;
+    uint8_t* sel = smem + kOffSel;
+    *reinterpret_cast<uint4*>(sel + sw32_offset(r, 0)) = make_uint4(kOne | (kOne << 16), kOne, 0u, 0u);
+    *reinterpret_cast<uint4*>(sel + sw32_offset(r, 1)) = make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(sel + kSelBytes + sw32_offset(r, 0)) =
+        make_uint4(0u, kOne << 16, kOne | (kOne << 16), 0u);
+    *reinterpret_cast<uint4*>(sel + kSelBytes + sw32_offset(r, 1)) = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();   // generic-proxy writes read by the tensor core
+  }
   if (warp == 4 && lane == 0) {
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
@@ -266,18 +288,17 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         }
         __syncwarp();
         ++j;
-        const int64_t rowbase = (int64_t)(w.b * a.H + w.h) * a.S;
+        const uint8_t* bias = p.bias + (int64_t)(w.b * a.H + w.h) * (a.S / 64) * kBiasBytes;
         for (int i = 0; i < w.n; ++i, ++g) {
           const int c = entries[w.e0 + i] & kEntryIdxMask;
           const int st = g % kKvStages;
           if (!warp_mbar_wait(&bars->ring_empty[st], ((g / kKvStages) & 1) ^ 1, abort)) { ok = false; break; }
           if (elect_one()) {
             uint8_t* sb = smem + kOffKvRing + st * kKvStageBytes;
-            mbar_arrive_expect_tx(&bars->ring_full[st], 2 * kChunkBytes + 512);
+            mbar_arrive_expect_tx(&bars->ring_full[st], 2 * kChunkBytes + kBiasBytes);
             tma_load_4d(sb, &tmQ, &bars->ring_full[st], 0, 64 * c, w.h, w.b);
             tma_load_4d(sb + kChunkBytes, &tmDO, &bars->ring_full[st], 0, 64 * c, w.h, w.b);
-            bulk_load(sb + 2 * kChunkBytes, p.nlse2 + rowbase + 64 * c, 256, &bars->ring_full[st]);
-            bulk_load(sb + 2 * kChunkBytes + 256, a.delta + rowbase + 64 * c, 256, &bars->ring_full[st]);
+            bulk_load(sb + 2 * kChunkBytes, bias + (int64_t)c * kBiasBytes, kBiasBytes, &bars->ring_full[st]);
           }
           __syncwarp();
         }
@@ -296,6 +317,9 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
       const uint64_t ptdesc = sw128_desc(smem_u32(smem + kOffPt), 16, 1024);
       const uint64_t dstdesc = sw128_desc(smem_u32(smem + kOffDSt), 16, 1024);
       const uint64_t ring0 = sw128_desc(smem_u32(smem + kOffKvRing), 16, 1024);
+      const uint64_t sel_lse = sw32_desc(smem_u32(smem + kOffSel), 256);
+      const uint64_t sel_dl = sw32_desc(smem_u32(smem + kOffSel + kSelBytes), 256);
+      const uint64_t bias0 = sw32_desc(smem_u32(smem + kOffKvRing + 2 * kChunkBytes), 256);
       uint32_t g = 0, j = 0;
       bool ok = true;
       auto issue_scores = [&](uint32_t gs) -> bool {
@@ -306,10 +330,13 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         if (elect_one()) {
           const uint64_t qd = ring0 + (uint64_t)((st * kKvStageBytes) >> 4);
           const uint64_t dod = ring0 + (uint64_t)((st * kKvStageBytes + kChunkBytes) >> 4);
+          const uint64_t bd = bias0 + (uint64_t)((st * kKvStageBytes) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) mma_bf16_ss(tmem + 0, kdesc + 2 * kk, qd + 2 * kk, kIdescQK, kk > 0);
+          mma_bf16_ss(tmem + 0, sel_lse, bd, kIdescQK, 1u);   // + (-lse / scale)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) mma_bf16_ss(tmem + 64, vdesc + 2 * kk, dod + 2 * kk, kIdescQK, kk > 0);
+          mma_bf16_ss(tmem + 64, sel_dl, bd, kIdescQK, 1u);   // - Dl
           mma_commit(&bars->s_full);
         }
         __syncwarp();
@@ -381,13 +408,9 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
         if (w.n > 0) {
           for (int i = 0; i < w.n; ++i, ++g) {
             const int32_t e = entries[w.e0 + i];
-            const int st = g % kKvStages;
-            const float4* nl4 = reinterpret_cast<const float4*>(smem + kOffKvRing + st * kKvStageBytes + 2 * kChunkBytes);
-            const float4* dl4 = nl4 + 16;
+            // S^T - lse/scale and dP^T - Dl (the bias MMAs): nothing per query is read here.
             if (!warp_mbar_wait(&bars->s_full, g & 1, abort)) { ok = false; break; }
             tc_fence_after();
-            // The chunk's -lse*log2e and Dl came with its TMA copies.
-            if (!warp_mbar_wait(&bars->ring_full[st], (g / kKvStages) & 1, abort)) { ok = false; break; }
             const bool act = (e & f_active) != 0;    // warp-uniform (a warp is inside one half)
             const bool dg = (e & f_diag) != 0;
             uint32_t ppa[2][16], pda[2][16];   // P^T and dS^T of this row, bf16 pairs
@@ -407,12 +430,11 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
               if (act) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
-                  const float4 nl = nl4[8 * hh + q], dl = dl4[8 * hh + q];
                   const int jq = 32 * hh + 4 * q;   // query index within the chunk
                   const int j0 = 4 * q;             // index within this half's registers
                   float x0, x1, x2, x3;
-                  upk2(fma2(pk2(__uint_as_float(sr[j0]), __uint_as_float(sr[j0 + 1])), cc2, pk2(nl.x, nl.y)), x0, x1);
-                  upk2(fma2(pk2(__uint_as_float(sr[j0 + 2]), __uint_as_float(sr[j0 + 3])), cc2, pk2(nl.z, nl.w)), x2, x3);
+                  upk2(mul2(pk2(__uint_as_float(sr[j0]), __uint_as_float(sr[j0 + 1])), cc2), x0, x1);
+                  upk2(mul2(pk2(__uint_as_float(sr[j0 + 2]), __uint_as_float(sr[j0 + 3])), cc2), x2, x3);
                   float p0 = ex2(x0), p1 = ex2(x1), p2 = ex2(x2), p3 = ex2(x3);
                   if (dg) {   // token-level causal cut: key kl is after query j
                     if (jq < kl) p0 = 0.f;
@@ -421,8 +443,8 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
                     if (jq + 3 < kl) p3 = 0.f;
                   }
                   float d0, d1, d2, d3;
-                  upk2(mul2(pk2(p0, p1), sub2(pk2(__uint_as_float(dr[j0]), __uint_as_float(dr[j0 + 1])), pk2(dl.x, dl.y))), d0, d1);
-                  upk2(mul2(pk2(p2, p3), sub2(pk2(__uint_as_float(dr[j0 + 2]), __uint_as_float(dr[j0 + 3])), pk2(dl.z, dl.w))), d2, d3);
+                  upk2(mul2(pk2(p0, p1), pk2(__uint_as_float(dr[j0]), __uint_as_float(dr[j0 + 1]))), d0, d1);
+                  upk2(mul2(pk2(p2, p3), pk2(__uint_as_float(dr[j0 + 2]), __uint_as_float(dr[j0 + 3]))), d2, d3);
                   pp[2 * q] = pack_bf16(p0, p1);
                   pp[2 * q + 1] = pack_bf16(p2, p3);
                   pd[2 * q] = pack_bf16(d0, d1);
@@ -757,9 +779,23 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
 }
 
 // =============================================================================== prep
+// Three bf16 parts whose sum is v to within fp32 rounding (each part takes the remainder).
+__device__ __forceinline__ void split3_bf16(float v, uint32_t (&h)[3]) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const __nv_bfloat16 b = __float2bfloat16_rn(v);
+    h[i] = (uint32_t)__bfloat16_as_ushort(b);
+    v -= __bfloat162float(b);
+  }
+}
+
 // Dl = rowsum(dO * O) and -lse * log2(e) (-inf for fully masked rows, whose lse is the
-// finfo.min fill) for every query row; 8 lanes per row, one 16-byte load of O and dO each.
-__global__ void __launch_bounds__(256) tc_bwd_prep_kernel(AttnArgs a, float* __restrict__ nlse2) {
+// finfo.min fill) for every query row, and the row's line of its chunk's bias operand (the dK/dV
+// kernel's extra MMAs): parts of -lse/scale at elements 0-2 (-1e30 for fully masked rows, finite
+// so that the selector's zeros never multiply an infinity) and of -Dl at 3-5; 8 lanes per row,
+// one 16-byte load of O and dO each.
+__global__ void __launch_bounds__(256) tc_bwd_prep_kernel(AttnArgs a, float* __restrict__ nlse2,
+                                                          uint8_t* __restrict__ bias) {
   const int64_t nrows = (int64_t)a.B * a.H * a.S;
   const int64_t row = (int64_t)blockIdx.x * 32 + (threadIdx.x >> 3);
   const int sub = threadIdx.x & 7;
@@ -787,7 +823,16 @@ __global__ void __launch_bounds__(256) tc_bwd_prep_kernel(AttnArgs a, float* __r
   if (row < nrows && sub == 0) {
     a.delta[row] = acc;
     const float l = a.lse[row];
-    nlse2[row] = (l == kMaskFill) ? -INFINITY : -l * kLog2e;
+    const bool empty = l == kMaskFill;
+    nlse2[row] = empty ? -INFINITY : -l * kLog2e;
+    uint32_t hl[3], hd[3];
+    split3_bf16(empty ? -1e30f : -l / a.scale, hl);
+    split3_bf16(-acc, hd);
+    uint8_t* line = bias + (row >> 6) * kBiasBytes;   // S is a multiple of 64 on this path
+    const int r = (int)(row & 63);
+    *reinterpret_cast<uint4*>(line + sw32_offset(r, 0)) =
+        make_uint4(hl[0] | (hl[1] << 16), hl[2] | (hd[0] << 16), hd[1] | (hd[2] << 16), 0u);
+    *reinterpret_cast<uint4*>(line + sw32_offset(r, 1)) = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
@@ -824,8 +869,9 @@ bool tc_attn_bwd_supported(const AttnArgs& a, int dtype) {
   return ok;
 }
 
-// Workspace: delta [B*H*S] | ucol [B*H*64] | -lse*log2e [B*H*S] | counters (256 B); each
-// section 256-byte aligned (the first two are shared with the CUDA-core backward).
+// Workspace: delta [B*H*S] | ucol [B*H*64] | -lse*log2e [B*H*S] | counters (256 B) | bias
+// operands [B*H*S/64][kBiasBytes]; each section 256-byte aligned (the first two are shared with
+// the CUDA-core backward).
 int tc_attn_bwd(const AttnArgs& a_in, void* ws, size_t ws_bytes, cudaStream_t s) {
   DeviceInfo di;
   int st = device_info(&di);
@@ -835,14 +881,17 @@ int tc_attn_bwd(const AttnArgs& a_in, void* ws, size_t ws_bytes, cudaStream_t s)
   AttnArgs a = a_in;
   const int64_t bh = (int64_t)a.B * a.H;
   const size_t s1 = align_up((size_t)(bh * a.S) * 4, 256), s2 = align_up((size_t)(bh * a.D) * 4, 256);
-  XSAKE_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= 2 * s1 + s2 + 256, XSAKE_EINVAL,
-                "the tensor-core backward needs a 256-byte aligned workspace of %zu bytes (got %zu)",
-                2 * s1 + s2 + 256, ws_bytes);
+  const size_t s_bias = (size_t)(bh * (a.S / 64)) * kBiasBytes;
+  const size_t need = 2 * s1 + s2 + 256 + s_bias;
+  XSAKE_REQUIRE(ws != nullptr && ((uintptr_t)ws & 255) == 0 && ws_bytes >= need, XSAKE_EINVAL,
+                "the tensor-core backward needs a 256-byte aligned workspace of %zu bytes (got %zu)", need,
+                ws_bytes);
   uint8_t* w = reinterpret_cast<uint8_t*>(ws);
   a.delta = reinterpret_cast<float*>(w);
   a.ucol = reinterpret_cast<float*>(w + s1);
   float* nlse2 = reinterpret_cast<float*>(w + s1 + s2);
   int* counters = reinterpret_cast<int*>(w + 2 * s1 + s2);
+  uint8_t* bias = w + 2 * s1 + s2 + 256;
 
   CUtensorMap mq, mk, mv, mdo, mq128, mdo128, mk128, mv128;
   if ((st = tc_make_map(&mq, a.q, a.qs, a.B, a.H, a.S, 64))) return st;
@@ -869,7 +918,7 @@ int tc_attn_bwd(const AttnArgs& a_in, void* ws, size_t ws_bytes, cudaStream_t s)
 
   XSAKE_CUDA_TRY(cudaMemsetAsync(counters, 0, 2 * sizeof(int), s));
   const int64_t nrows = bh * a.S;
-  tc_bwd_prep_kernel<<<(unsigned)((nrows + 31) / 32), 256, 0, s>>>(a, nlse2);
+  tc_bwd_prep_kernel<<<(unsigned)((nrows + 31) / 32), 256, 0, s>>>(a, nlse2, bias);
   if ((st = check_launch("tc_bwd_prep_kernel"))) return st;
   tc_ucol_kernel<<<(unsigned)bh, 64, 0, s>>>(a);
   if ((st = check_launch("tc_ucol_kernel"))) return st;
@@ -878,6 +927,7 @@ int tc_attn_bwd(const AttnArgs& a_in, void* ws, size_t ws_bytes, cudaStream_t s)
   p.a = a;
   p.scale_log2 = a.scale * kLog2e;
   p.nlse2 = nlse2;
+  p.bias = bias;
   p.counter = counters;
   const int grid = std::max(1, std::min(a.L.nitems, 2 * di.sm_count));
   tc_bwd_dkdv_kernel<<<grid, kThreads, kKvSmemBytes, s>>>(mk128, mv128, mq, mdo, p);

@@ -234,6 +234,26 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr, uint32_t lbo_
   return d;
 }
 
+// Shared-memory matrix descriptor, SWIZZLE_32B K-major layout: rows of 32 bytes (16 bf16, one
+// K=16 slice), 8-row groups `sbo_bytes` apart, the 16-byte chunk index of row r XOR (r >> 2) & 1
+// (sw32_offset); start address 256-aligned.  Layout type 6 = SWIZZLE_32B; the leading byte offset
+// is unused by swizzled K-major layouts.
+__device__ __forceinline__ uint64_t sw32_desc(uint32_t smem_addr, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)6 << 61;
+  return d;
+}
+
+// Byte offset of 16-byte chunk `chunk` (0 or 1) of row r in a SWIZZLE_32B K-major block whose
+// 8-row groups are 256 bytes apart.
+__host__ __device__ constexpr uint32_t sw32_offset(int r, int chunk) {
+  return (uint32_t)((r >> 3) * 256 + (r & 7) * 32 + ((chunk ^ ((r >> 2) & 1)) << 4));
+}
+
 // Instruction descriptor of kind::f16 with bf16 A/B, fp32 D.
 // [4,6) D format (1 = F32), [7,10) A format (1 = BF16), [10,13) B format (1 = BF16),
 // [15] A major (0 = K), [16] B major (0 = K, 1 = MN), [17,23) N>>3, [24,29) M>>4.
