@@ -65,10 +65,13 @@ static_assert(kKvStageBytes % 1024 == 0 && kOffKvRing % 1024 == 0, "SWIZZLE_128B
 constexpr int kOffKvBar = kOffKvRing + kKvStages * kKvStageBytes;
 
 // ---- dQ kernel shared memory
-constexpr int kQStages = 3;
+constexpr int kQStages = 4;
 constexpr int kQStageBytes = 2 * kChunkBytes;               // K, V
-constexpr int kOffQ = 0, kOffDO = kTileBytes, kOffDS = 2 * kTileBytes;
-constexpr int kOffQRing = 3 * kTileBytes;
+constexpr int kOffQ = 0, kOffDO = kTileBytes;
+constexpr int kOffQRing = 2 * kTileBytes;
+// dQ kernel TMEM: S [0, 64), dP [64, 128), dQ [128, 192), dS (bf16 pairs, the dQ MMA's A operand)
+// double-buffered at [192, 224) and [224, 256).
+constexpr uint32_t kDsCol = 192;
 constexpr int kOffQBar = kOffQRing + kQStages * kQStageBytes;
 
 template <int NS>
@@ -77,7 +80,8 @@ struct BwdBars {
   uint64_t tile_full, tile_empty;          // the resident 128-row operands of the item
   uint64_t ring_full[NS], ring_empty[NS];  // per-chunk operands
   uint64_t s_full, s_free;                 // score-like products in TMEM
-  uint64_t p_full, p_free;                 // bf16 operands written by the elementwise warps
+  uint64_t p_full[2], p_free[2];           // bf16 operands written by the elementwise warps (dK/dV:
+                                           // one buffer, index 0; dQ: dS buffers of even / odd steps)
   uint64_t acc_full, acc_free;             // accumulators of one item
   uint64_t drain;
 };
@@ -129,8 +133,10 @@ __device__ void init_bars(BwdBars<NS>* bars) {
   }
   mbar_init(&bars->s_full, 1);
   mbar_init(&bars->s_free, 128);
-  mbar_init(&bars->p_full, 128);
-  mbar_init(&bars->p_free, 1);
+  for (int b = 0; b < 2; ++b) {
+    mbar_init(&bars->p_full[b], 128);
+    mbar_init(&bars->p_free[b], 1);
+  }
   mbar_init(&bars->acc_full, 1);
   mbar_init(&bars->acc_free, 128);
   mbar_init(&bars->drain, 1);
@@ -344,7 +350,7 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
       };
       auto issue_acc = [&](uint32_t gs, bool first) -> bool {
         const int st = gs % kKvStages;
-        if (!warp_mbar_wait(&bars->p_full, gs & 1, abort)) return false;
+        if (!warp_mbar_wait(&bars->p_full[0], gs & 1, abort)) return false;
         if (first && j > 0 && !warp_mbar_wait(&bars->acc_free, (j - 1) & 1, abort)) return false;
         tc_fence_after();
         if (elect_one()) {
@@ -358,7 +364,7 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
           for (int kk = 0; kk < 4; ++kk)   // dK += dS^T Q
             mma_bf16_ss(tmem + 192, dstdesc + 2 * kk, qd + (uint64_t)((2048 * kk) >> 4), kIdescAcc,
                         (first && kk == 0) ? 0u : 1u);
-          mma_commit(&bars->p_free);
+          mma_commit(&bars->p_free[0]);
           mma_commit(&bars->ring_empty[st]);
         }
         __syncwarp();
@@ -457,7 +463,7 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             }
             // Computed into registers first: the wait for the previous chunk's accumulation to
             // release P^T / dS^T overlaps the exponentials above.
-            if (g > 0 && !warp_mbar_wait(&bars->p_free, (g - 1) & 1, abort)) { ok = false; break; }
+            if (g > 0 && !warp_mbar_wait(&bars->p_free[0], (g - 1) & 1, abort)) { ok = false; break; }
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
               store_sw128_half(ptrow, rsw, hh, ppa[hh]);
@@ -465,7 +471,7 @@ tc_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constan
             }
             fence_proxy_async_smem();
             tc_fence_before();
-            mbar_arrive(&bars->p_full);
+            mbar_arrive(&bars->p_full[0]);
           }
           if (!ok) break;
           if (!warp_mbar_wait(&bars->acc_full, j & 1, abort)) { ok = false; break; }
@@ -606,7 +612,6 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       // ------------------------------------------------------------------ MMA issuer
       const uint64_t qdesc = sw128_desc(smem_u32(smem + kOffQ), 16, 1024);
       const uint64_t dodesc = sw128_desc(smem_u32(smem + kOffDO), 16, 1024);
-      const uint64_t dsdesc = sw128_desc(smem_u32(smem + kOffDS), 16, 1024);
       const uint64_t ring0 = sw128_desc(smem_u32(smem + kOffQRing), 16, 1024);
       uint32_t g = 0, j = 0;
       bool ok = true;
@@ -629,16 +634,19 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       };
       auto issue_acc = [&](uint32_t gs, bool first) -> bool {
         const int st = gs % kQStages;
-        if (!warp_mbar_wait(&bars->p_full, gs & 1, abort)) return false;
+        // dS of step gs sits in TMEM buffer gs & 1; each buffer's barriers complete once per two
+        // steps, so their parity waits stay unambiguous with the elementwise warps a step ahead.
+        if (!warp_mbar_wait(&bars->p_full[gs & 1], (gs >> 1) & 1, abort)) return false;
         if (first && j > 0 && !warp_mbar_wait(&bars->acc_free, (j - 1) & 1, abort)) return false;
         tc_fence_after();
         if (elect_one()) {
           const uint64_t kd = ring0 + (uint64_t)((st * kQStageBytes) >> 4);
+          const uint32_t ds = tmem + kDsCol + 32 * (gs & 1);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)   // dQ += dS K
-            mma_bf16_ss(tmem + 128, dsdesc + 2 * kk, kd + (uint64_t)((2048 * kk) >> 4), kIdescAcc,
+          for (int kk = 0; kk < 4; ++kk)   // dQ += dS K, dS (A) from TMEM
+            mma_bf16_ts(tmem + 128, ds + 8 * kk, kd + (uint64_t)((2048 * kk) >> 4), kIdescAcc,
                         (first && kk == 0) ? 0u : 1u);
-          mma_commit(&bars->p_free);
+          mma_commit(&bars->p_free[gs & 1]);
           mma_commit(&bars->ring_empty[st]);
         }
         __syncwarp();
@@ -674,8 +682,6 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
       const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
       const int32_t f_active = half ? kFlagActive1 : kFlagActive0;
       const int32_t f_diag = half ? kFlagDiag1 : kFlagDiag0;
-      const int rsw = row & 7;
-      uint8_t* dsrow = smem + kOffDS + (row >> 3) * 1024 + rsw * 128;
       const uint64_t cc2 = pk2(p.scale_log2, p.scale_log2);
       uint32_t g = 0, j = 0;
       bool ok = true;
@@ -732,14 +738,15 @@ tc_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant_
                 for (int q = 0; q < 16; ++q) pd[q] = 0u;
               }
             }
-            // Computed into registers first: the wait for the previous chunk's dQ MMA to release
-            // dS overlaps the exponentials above.
-            if (g > 0 && !warp_mbar_wait(&bars->p_free, (g - 1) & 1, abort)) { ok = false; break; }
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) store_sw128_half(dsrow, rsw, hh, pda[hh]);
-            fence_proxy_async_smem();
+            // Computed into registers first; the dS buffer of this step was last read by the dQ
+            // MMA of step g - 2.
+            if (g > 1 && !warp_mbar_wait(&bars->p_free[g & 1], ((g - 2) >> 1) & 1, abort)) { ok = false; break; }
+            const uint32_t ds = tmem + lane_base + kDsCol + 32 * (g & 1);
+            XSAKE_TMEM_ST16(ds, pda[0]);
+            XSAKE_TMEM_ST16(ds + 16, pda[1]);
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&bars->p_full);
+            mbar_arrive(&bars->p_full[g & 1]);
           }
           if (!ok) break;
           if (!warp_mbar_wait(&bars->acc_full, j & 1, abort)) { ok = false; break; }
