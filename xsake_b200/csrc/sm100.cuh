@@ -202,25 +202,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]) \
       : "memory")
 
-// 16 columns of 32-bit elements of this warp's 32 lanes (thread i <- lane base + i).
-#define XSAKE_TMEM_LD16(taddr, r)                                                               \
-  asm volatile(                                                                                 \
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"  \
-      "%14,%15}, [%16];"                                                                        \
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),      \
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),  \
-        "=r"(r[14]), "=r"(r[15])                                                                \
-      : "r"(taddr))
-
-// tcgen05.wait::ld naming the 16 destination registers of a preceding XSAKE_TMEM_LD16.
-#define XSAKE_TMEM_WAIT_LD16(r)                                                                 \
-  asm volatile("tcgen05.wait::ld.sync.aligned;"                                                 \
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),         \
-                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),       \
-                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])                              \
-               :                                                                                 \
-               : "memory")
-
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // tcgen05.wait::ld that also names the 32 destination registers of a preceding load as
