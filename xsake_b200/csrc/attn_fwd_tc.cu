@@ -835,8 +835,10 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
     }
   } else if (warp == 10 || warp == 11) {
     // ------------------------------------------------------------------ MMA issuers
-    // Per step: one combined wait (both units' K/V slots landed, P of step s-3 written), then
-    // PV(s-3) for both units and QK(s) for both units, as in tc_fwd_kernel.
+    // Per step: one combined wait (K(s) landed; P(s-2) written and V(s-2) landed), then PV(s-2)
+    // and QK(s) for both units.  This warp's loop is on the softmax's critical path (it shares its
+    // sub-partition with two busy softmax warps), so it carries as few instructions as possible:
+    // one combined wait and no walk of the entry list (A/B: 117.1 vs 128.1 us).
     const int X = warp - 10;
     volatile int* item_slot = item_slots + 2 * X;
     const uint32_t tcol = tmem + 256 * X;
@@ -844,12 +846,13 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
     uint32_t qk = 0, steps = 0, pvs = 0, titems = 0, item_first = 0;
     bool solo = false;                  // the current item (PVs never cross an item)
     bool ok = true;
-    // PV of step s (both units) from V stage s % kPairVStages; the caller has waited for P(s),
-    // V(s) and, on an item's first PV, for the epilogue to have read the previous item's O.
-    auto emit_pv = [&](uint32_t s, bool first) {
+    // PV of step s (both units) from V stage s % kPairVStages, issued by the elected lane; the
+    // caller has waited for P(s), V(s) and, on an item's first PV, for the epilogue to have read
+    // the previous item's O.
+    auto pv_mmas = [&](uint32_t s, bool first) {
       const uint32_t sbuf = s % 3;
       const int vs = kPairKStages + (int)(s % kPairVStages);
-      if (elect_one()) {
+      {
         const uint64_t va = kdesc0 + (uint64_t)((vs * kStageBytes) >> 4);
         const uint64_t vb = va + (uint64_t)(kKBytes >> 4);
 #pragma unroll
@@ -865,7 +868,6 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
         mma_commit(&bars->o_done[X][s & 1]);
         mma_commit(&bars->kv_empty[X][vs]);
       }
-      __syncwarp();
     };
     auto issue_pv = [&]() -> bool {
       const uint32_t s = pvs;
@@ -875,17 +877,18 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       const bool first = (s == item_first);
       if (first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) return false;
       tc_fence_after();
-      emit_pv(s, first);
+      if (elect_one()) pv_mmas(s, first);
+      __syncwarp();
       ++pvs;
       return true;
     };
-    // Taking an item reads its work entry, its step count and its first 32 entries (dependent
-    // global loads).  The next item is taken while this item's last PVs wait for their P, when the
-    // scheduler has already published it, so its first QK follows the last PV directly.
+    // Taking an item reads its work entry and counts its steps (the MMAs need nothing else of
+    // the entry list: K and V stages follow the step index).  The next item is taken while this
+    // item's last PVs wait for their P, when the scheduler has already published it, so its
+    // first QK follows the last PV directly.
     struct Taken {
-      int item, cnt, last;
+      int item, cnt;
       PItem w;
-      int32_t held;   // entries [0, 32) of the item, lane j holding entry j
     };
     auto take = [&](uint32_t kk, Taken& t) -> bool {
       const int slot = kk & 1;
@@ -897,8 +900,8 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       t.cnt = 0;
       if (t.item >= 0) {
         t.w = decode_pair(a, t.item);
-        t.cnt = count_steps(entries, t.w.e0, t.w.n, (t.w.j & 1) ? kFlagActive1 : kFlagActive0, t.last);
-        t.held = lane < t.w.n ? entries[t.w.e0 + lane] : 0;
+        int last = -1;
+        t.cnt = count_steps(entries, t.w.e0, t.w.n, (t.w.j & 1) ? kFlagActive1 : kFlagActive0, last);
       }
       return true;
     };
@@ -915,8 +918,6 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       if (cur.item < 0) break;
       if (cur.cnt == 0) continue;
       const PItem& w = cur.w;
-      const int32_t fa = (w.j & 1) ? kFlagActive1 : kFlagActive0;
-      const int last_used = cur.last;
       const int qs = qk % kQSlots;
       if (!warp_mbar_wait(&bars->q_full[X][qs], (qk / kQSlots) & 1, abort)) { ok = false; break; }
       ++qk;
@@ -924,11 +925,8 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
       const uint64_t qda = sw128_desc(qaddr, 16, 1024), qdb = sw128_desc(qaddr + kQBytes / 2, 16, 1024);
       item_first = steps;
       solo = w.solo;
-      int32_t held = cur.held;
-      int base = 0;
-      for (int i = 0; i < w.n && ok; ++i) {
-        const int32_t e = entry_at(entries, w, i, held, base);
-        if (!(e & fa)) continue;
+      // The MMAs need only the step count: K and V stages follow the step index.
+      for (int t = 0; t < cur.cnt && ok; ++t) {
         const int ks = steps % kPairKStages;
         while (ok && pvs + kPairPvLag < steps) ok = issue_pv();
         if (!ok) break;
@@ -936,14 +934,13 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
         const uint32_t ps = pvs;
         const bool pv_first = pv_now && ps == item_first;
         if (pv_first && titems > 0 && !warp_mbar_wait(&bars->o_free[X], (titems - 1) & 1, abort)) { ok = false; break; }
-        if (!warp_mbar_wait2(&bars->kv_full[X][ks], (steps / kPairKStages) & 1, &bars->p_full[X][ps % 3],
-                             (ps / 3) & 1, pv_now, abort) ||
-            (pv_now && !warp_mbar_wait(&bars->kv_full[X][kPairKStages + ps % kPairVStages],
-                                       (ps / kPairVStages) & 1, abort))) { ok = false; break; }
+        if (!warp_mbar_wait3(&bars->kv_full[X][ks], (steps / kPairKStages) & 1, &bars->p_full[X][ps % 3],
+                             (ps / 3) & 1, &bars->kv_full[X][kPairKStages + ps % kPairVStages],
+                             (ps / kPairVStages) & 1, pv_now, abort)) { ok = false; break; }
         const uint32_t sb = steps % 3;
         tc_fence_after();
-        if (pv_now) emit_pv(ps, pv_first);
         if (elect_one()) {
+          if (pv_now) pv_mmas(ps, pv_first);
           const uint64_t ka = kdesc0 + (uint64_t)((ks * kStageBytes) >> 4);
           const uint64_t kb = ka + (uint64_t)(kKBytes >> 4);
 #pragma unroll
@@ -956,7 +953,7 @@ __device__ __forceinline__ void pair_roles(const CUtensorMap& tmQ, const CUtenso
           }
           mma_commit(&bars->s_full[X][sb]);
           mma_commit(&bars->kv_empty[X][ks]);
-          if (i == last_used) mma_commit(&bars->q_empty[X][qs]);
+          if (t == cur.cnt - 1) mma_commit(&bars->q_empty[X][qs]);
         }
         __syncwarp();
         if (pv_now) ++pvs;

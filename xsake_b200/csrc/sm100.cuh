@@ -81,6 +81,20 @@ __device__ __forceinline__ bool warp_mbar_wait2(uint64_t* b1, uint32_t p1, uint6
   return __all_sync(0xffffffffu, ok);
 }
 
+// Warp-uniform wait for one barrier phase and, if `need23`, two more: all probes go out before
+// any result is used.
+__device__ __forceinline__ bool warp_mbar_wait3(uint64_t* b1, uint32_t p1, uint64_t* b2, uint32_t p2, uint64_t* b3,
+                                                uint32_t p3, bool need23, volatile int* abort) {
+  const bool r1 = mbar_try_wait(b1, p1);
+  const bool r2 = need23 ? mbar_try_wait(b2, p2) : true;
+  const bool r3 = need23 ? mbar_try_wait(b3, p3) : true;
+  bool ok = true;
+  if (!r1) ok = mbar_wait(b1, p1, abort);
+  if (ok && !r2) ok = mbar_wait(b2, p2, abort);
+  if (ok && !r3) ok = mbar_wait(b3, p3, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // One lane of a converged warp (elect.sync): lets a whole warp run the uniform control flow
 // of a single-issuer role while exactly one lane issues the tcgen05 / TMA instructions.
 __device__ __forceinline__ bool elect_one() {
