@@ -15,7 +15,8 @@ This package restates, in NumPy, the algorithms of the reference project
 
 Who may use it: only ``tests/``, ``__graft_entry__.smoke()`` and the
 ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py``, and there only as
-the checker or as the timed CPU baseline.  The product package ``xsake_b200``
+the expected results that GPU outputs are compared against, or as the timed CPU
+baseline.  The product package ``xsake_b200``
 never imports this package; its compute path is CUDA only.
 
 Pinning: the reference's own tests hold no stored vectors.  The golden files
